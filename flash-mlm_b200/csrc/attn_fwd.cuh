@@ -1,0 +1,560 @@
+// Bidirectional MLM attention forward for sm_100a (B200).
+//
+// Semantics follow the reference Triton kernels:
+//   * src/flash_mlm/mlm_kernel_impl.py:10-62   (_mlm_inner_attention: masked online softmax)
+//   * src/flash_mlm/mlm_kernel_impl.py:65-216  (_mlm_main_kernel_impl: dense [B,H,N,D])
+//   * src/flash_mlm/mlm_kernel_impl.py:219-390 (_mlm_compressed_kernel_impl: packed varlen,
+//     context segment then main segment, causal_query_seq_attn prefix, MLA)
+// Every query row attends to [context segment] ++ [main segment]; rows with no
+// key at all produce zeros (l_safe, mlm_kernel_impl.py:381).
+//
+// Design (one persistent CTA per SM, warp specialised):
+//   warps [0, 4*NQ)   softmax warpgroups, one per 128-row query tile; each
+//                     thread owns one query row (one TMEM lane)
+//   warp 4*NQ         TMA producer (Q tiles, K/V blocks through a STAGES ring)
+//   warp 4*NQ+1       TMEM allocator + single-thread tcgen05.mma issuer
+// A work item is NQ query tiles of 128 rows from the same (sequence, head);
+// they share every K/V block.  S = Q K^T lands in TMEM (fp32), softmax reads
+// it with tcgen05.ld, writes P (f16/bf16) back over S, and O += P V is issued
+// with P as the TMEM operand.  The running max is only moved (and O rescaled
+// in TMEM) when a new block raises it by more than 2^8, which keeps P <= 256.
+// MMA order per block j is  PV_t(j), S_t(j+1)  for each tile t, so when the
+// softmax sees S_t(j+1) complete, PV_t(j) is complete too (tcgen05 ops issued
+// by one thread complete in order and a commit covers all earlier ops).
+#pragma once
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "ptx.cuh"
+
+namespace fmlm {
+
+// Error codes written to the device error word.
+enum : int { kErrTimeout = 1 };
+
+struct AttnParams {
+  int mode;         // 0 = dense [B,H,N,D] rows; 1 = packed variable-length (cu_seqlens_q)
+  int q_padded;     // packed: Q rows come from a padded [B,H,N,D] tensor (1) or packed [H*Tq,D] (0)
+  int main_padded;  // packed: main K/V rows from padded [B,Hkv,N,D] (1) or packed [Hkv*Tk,D] (0)
+  int causal;       // packed: main range is the prefix [0, cu_q[b+1]) (causal_query_seq_attn)
+  int has_ctx;      // a context segment is attended (prefill=False and context rows exist)
+  int is_mla;       // V is the K tile; K/V head coordinate is 0 (except dense main keys)
+  int B, H, N;      // N: dense / padded sequence length
+  int ctx_bs;       // context batch size
+  int ctx_len;      // dense: uniform context length per context batch
+  long long t_out;  // packed: rows per head in the output
+  int num_items;    // dense: number of work items
+  float scale_log2; // scale * log2(e)
+  const int* cu_q;  // [B+1] packed query offsets
+  const int* cu_kv; // context offsets (packed)
+  const int* work;  // packed: [0] = entry count, [1..] = (b << 16 | pair) entries
+  void* out;        // [rows, D]
+  int* err;         // device error word
+  unsigned long long timeout_ns;
+};
+
+template <int D_, int NQ_>
+struct AttnCfg {
+  static constexpr int D = D_;
+  static constexpr int NQ = NQ_;
+  static constexpr int BM = 128;                   // query rows per tile (UMMA M)
+  static constexpr int BN = (D >= 256) ? 64 : 128; // key rows per block (UMMA N of S)
+  static constexpr int PAIR = NQ * BM;             // query rows per work item
+  static constexpr int SWB = (D * 2 >= 128) ? 128 : D * 2;  // swizzle span in bytes
+  static constexpr int SLAB_COLS = SWB / 2;
+  static constexpr int NSLAB = D / SLAB_COLS;
+  static constexpr int Q_BYTES = BM * D * 2;
+  static constexpr int KV_BYTES = BN * D * 2;
+  static constexpr int STAGES = (D <= 32) ? 4 : (D <= 64) ? 3 : 2;
+  static constexpr int NUM_SOFTMAX_WARPS = 4 * NQ;
+  static constexpr int TMA_WARP = NUM_SOFTMAX_WARPS;
+  static constexpr int MMA_WARP = NUM_SOFTMAX_WARPS + 1;
+  static constexpr int THREADS = 32 * (NUM_SOFTMAX_WARPS + 2);
+  static constexpr int MAX_REGS = (65536 / THREADS) / 8 * 8 > 255 ? 255 : (65536 / THREADS) / 8 * 8;
+  static constexpr int TM_S = 0;                   // S_t at column t*BN
+  static constexpr int TM_O = NQ * BN;             // O_t at column TM_O + t*D
+  static constexpr int TMEM_USED = NQ * (BN + D);
+  static constexpr int TMEM_COLS = TMEM_USED <= 32 ? 32 : TMEM_USED <= 64 ? 64 : TMEM_USED <= 128 ? 128
+                                 : TMEM_USED <= 256 ? 256 : 512;
+  static_assert(TMEM_USED <= 512, "TMEM budget");
+  static constexpr int SMEM_TILES = NQ * Q_BYTES + 2 * STAGES * KV_BYTES;
+  static constexpr int SMEM_BYTES = SMEM_TILES + 1024 /*barriers*/ + 1024 /*alignment*/;
+};
+
+struct Seg {
+  int map;  // 0 = context tensors, 1 = main tensors
+  int h, b; // head / batch coordinates in that tensor map
+  int row0, row1;
+  int fix;  // rows past row1 inside the tensor are caller padding: zero them in V
+  int nblk;
+};
+
+// One work item: up to two 128-row query tiles of one (sequence, head) and the
+// two key segments they attend (context, then main).  Kept as scalars so no
+// role needs dynamically indexed local memory.
+struct Item {
+  int qb, qh, qrow0;
+  int qrows0, qrows1;
+  long long out_row0;
+  Seg ctx, main;
+  __device__ __forceinline__ int qrows(int t) const { return t == 0 ? qrows0 : qrows1; }
+  __device__ __forceinline__ int nblocks() const { return ctx.nblk + main.nblk; }
+  // Segment and first row of key block j (j counts context blocks first).
+  __device__ __forceinline__ Seg block_seg(int j, int bn, int& row) const {
+    const bool in_ctx = j < ctx.nblk;
+    const Seg s = in_ctx ? ctx : main;
+    row = s.row0 + (in_ctx ? j : j - ctx.nblk) * bn;
+    return s;
+  }
+};
+
+template <int PAIR, int BN>
+__device__ __forceinline__ Item decode_item(const AttnParams& p, int w) {
+  Item it;
+  const int h = w % p.H;
+  const int r = w / p.H;
+  int b, pair, L, seq_start;
+  if (p.mode == 0) {
+    const int npairs = (p.N + PAIR - 1) / PAIR;
+    pair = r % npairs;
+    b = r / npairs;
+    L = p.N;
+    seq_start = 0;
+  } else {
+    const int e = __ldg(p.work + 1 + r);
+    b = e >> 16;
+    pair = e & 0xFFFF;
+    seq_start = __ldg(p.cu_q + b);
+    L = __ldg(p.cu_q + b + 1) - seq_start;
+  }
+  const int rel0 = pair * PAIR;
+  it.qh = h;
+  it.qrows0 = min(max(L - rel0, 0), 128);
+  it.qrows1 = min(max(L - rel0 - 128, 0), 128);
+  if (p.mode == 0) {
+    it.qb = b;
+    it.qrow0 = rel0;
+    it.out_row0 = ((long long)b * p.H + h) * p.N + rel0;
+  } else {
+    it.qb = p.q_padded ? b : 0;
+    it.qrow0 = p.q_padded ? rel0 : seq_start + rel0;
+    it.out_row0 = (long long)h * p.t_out + seq_start + rel0;
+  }
+  const int kh = p.is_mla ? 0 : h;
+  // context segment
+  Seg& c = it.ctx;
+  c.map = 0; c.h = kh; c.fix = 0;
+  if (!p.has_ctx) {
+    c.b = 0; c.row0 = 0; c.row1 = 0;
+  } else if (p.mode == 0) {
+    c.b = (p.ctx_bs > 1) ? b : 0; c.row0 = 0; c.row1 = p.ctx_len;
+  } else {
+    const int ci = (p.ctx_bs > 1) ? b : 0;
+    c.b = 0; c.row0 = __ldg(p.cu_kv + ci); c.row1 = __ldg(p.cu_kv + ci + 1);
+  }
+  // main segment
+  Seg& m = it.main;
+  m.map = 1; m.fix = 0;
+  if (p.mode == 0) {
+    m.h = h;  // dense MLA attends the per-head keys (mlm_kernel_impl.py:124, :188-206)
+    m.b = b; m.row0 = 0; m.row1 = p.N;
+  } else if (p.main_padded) {
+    m.h = kh; m.b = b; m.row0 = 0; m.row1 = L; m.fix = (L < p.N);
+  } else {
+    m.h = kh; m.b = 0; m.row0 = p.causal ? 0 : seq_start; m.row1 = seq_start + L;
+  }
+  c.nblk = c.row1 > c.row0 ? (c.row1 - c.row0 + BN - 1) / BN : 0;
+  m.nblk = m.row1 > m.row0 ? (m.row1 - m.row0 + BN - 1) / BN : 0;
+  return it;
+}
+
+struct __align__(8) AttnBarriers {
+  uint64_t q_full, q_empty, fix;
+  uint64_t k_full[4], v_full[4], kv_empty[4];
+  uint64_t s_full[2], p_full[2], o_full[2], o_empty[2];
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
+template <int D, int NQ, bool BF16>
+__global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<D, NQ>::MAX_REGS))
+    attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                    const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_kc,
+                    const __grid_constant__ CUtensorMap tm_vc, const AttnParams p) {
+  using C = AttnCfg<D, NQ>;
+  using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
+  constexpr int BM = C::BM, BN = C::BN, SWB = C::SWB, STAGES = C::STAGES;
+  constexpr int OC = (D >= 32) ? 32 : 16;  // O columns per TMEM transfer
+  auto tmem_ld_chunk = [](uint32_t a, uint32_t(&o)[OC]) {
+    if constexpr (OC == 32) tmem_ld_x32(a, o); else tmem_ld_x16(a, o);
+  };
+  auto tmem_st_chunk = [](uint32_t a, const uint32_t(&o)[OC]) {
+    if constexpr (OC == 32) tmem_st_x32(a, o); else tmem_st_x16(a, o);
+  };
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;
+  uint8_t* sK = sQ + NQ * C::Q_BYTES;
+  uint8_t* sV = sK + STAGES * C::KV_BYTES;
+  AttnBarriers* bar = reinterpret_cast<AttnBarriers*>(sV + STAGES * C::KV_BYTES);
+  volatile int* abort_flag = &bar->abort_flag;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const bool mla = p.is_mla != 0;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bar->q_full, 1);
+    mbar_init(&bar->q_empty, 1);
+    mbar_init(&bar->fix, 1);
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&bar->k_full[s], 1);
+      mbar_init(&bar->v_full[s], 1);
+      mbar_init(&bar->kv_empty[s], 1);
+    }
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(&bar->s_full[t], 1);
+      mbar_init(&bar->p_full[t], 4);
+      mbar_init(&bar->o_full[t], 1);
+      mbar_init(&bar->o_empty[t], 4);
+    }
+    bar->abort_flag = 0;
+    mbar_fence_init();
+  }
+  if (warp == C::MMA_WARP) {
+    tmem_alloc(&bar->tmem_base, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  if (warp == C::TMA_WARP && lane == 0) {
+    tma_prefetch_desc(&tm_q);
+    tma_prefetch_desc(&tm_k);
+    tma_prefetch_desc(&tm_v);
+    tma_prefetch_desc(&tm_kc);
+    tma_prefetch_desc(&tm_vc);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = bar->tmem_base;
+
+  const int num_items = (p.mode == 0) ? p.num_items : __ldg(p.work) * p.H;
+  const uint64_t tmo = p.timeout_ns;
+  bool failed = false;
+
+  auto fail = [&]() {
+    failed = true;
+    *abort_flag = 1;
+    atomicExch(p.err, kErrTimeout);
+  };
+
+  if (warp == C::TMA_WARP) {
+    // ------------------------------------------------------------ producer
+    uint32_t q_empty_ph = 1, fix_ph = 0;
+    uint32_t fill = 0;
+    for (int w = blockIdx.x; w < num_items && !failed; w += gridDim.x) {
+      const Item it = decode_item<C::PAIR, BN>(p, w);
+      if (lane == 0) {
+        if (!mbar_wait(&bar->q_empty, q_empty_ph, abort_flag, tmo)) fail();
+        q_empty_ph ^= 1;
+        if (!failed) {
+          const uint32_t nq = (it.qrows0 > 0 ? 1u : 0u) + (NQ > 1 && it.qrows1 > 0 ? 1u : 0u);
+          mbar_arrive_expect_tx(&bar->q_full, nq * C::Q_BYTES);
+#pragma unroll
+          for (int t = 0; t < NQ; ++t) {
+            if (it.qrows(t) == 0) continue;
+            for (int s = 0; s < C::NSLAB; ++s)
+              tma_load_4d(sQ + t * C::Q_BYTES + s * (BM * SWB), &tm_q, &bar->q_full, s * C::SLAB_COLS,
+                          it.qrow0 + t * BM, it.qh, it.qb);
+          }
+        }
+      }
+      failed = __shfl_sync(0xffffffffu, failed, 0);
+      const int nb = it.nblocks();
+      for (int j = 0; j < nb && !failed; ++j, ++fill) {
+        {
+          int row;
+          const Seg sgm = it.block_seg(j, BN, row);
+          const CUtensorMap* mk = sgm.map == 0 ? &tm_kc : &tm_k;
+          const CUtensorMap* mv = sgm.map == 0 ? &tm_vc : &tm_v;
+          const int st = fill % STAGES;
+          const uint32_t ph = (fill / STAGES) & 1u;
+          const int valid = min(BN, sgm.row1 - row);
+          const bool fix = sgm.fix && valid < BN;
+          uint8_t* tk = sK + st * C::KV_BYTES;
+          uint8_t* tv = sV + st * C::KV_BYTES;
+          if (lane == 0) {
+            if (!mbar_wait(&bar->kv_empty[st], ph ^ 1u, abort_flag, tmo)) fail();
+            if (!failed) {
+              if (!(fix && mla)) {
+                mbar_arrive_expect_tx(&bar->k_full[st], C::KV_BYTES);
+                for (int s = 0; s < C::NSLAB; ++s)
+                  tma_load_4d(tk + s * (BN * SWB), mk, &bar->k_full[st], s * C::SLAB_COLS, row, sgm.h, sgm.b);
+              }
+              if (fix) {
+                uint8_t* tf = mla ? tk : tv;
+                const CUtensorMap* mf = mla ? mk : mv;
+                mbar_arrive_expect_tx(&bar->fix, C::KV_BYTES);
+                for (int s = 0; s < C::NSLAB; ++s)
+                  tma_load_4d(tf + s * (BN * SWB), mf, &bar->fix, s * C::SLAB_COLS, row, sgm.h, sgm.b);
+              } else if (!mla) {
+                mbar_arrive_expect_tx(&bar->v_full[st], C::KV_BYTES);
+                for (int s = 0; s < C::NSLAB; ++s)
+                  tma_load_4d(tv + s * (BN * SWB), mv, &bar->v_full[st], s * C::SLAB_COLS, row, sgm.h, sgm.b);
+              }
+            }
+          }
+          failed = __shfl_sync(0xffffffffu, failed, 0);
+          if (fix && !failed) {
+            // Rows [valid, BN) of this V tile hold the caller's padding, which
+            // may be non-finite; P is zero there but 0 * NaN is not, so clear them.
+            if (!mbar_wait(&bar->fix, fix_ph, abort_flag, tmo)) fail();
+            fix_ph ^= 1u;
+            failed = __any_sync(0xffffffffu, failed);
+            if (!failed) {
+              uint8_t* tf = mla ? tk : tv;
+              const int nbytes = (BN - valid) * SWB;
+              for (int s = 0; s < C::NSLAB; ++s) {
+                uint4* z = reinterpret_cast<uint4*>(tf + s * (BN * SWB) + valid * SWB);
+                for (int i = lane; i < nbytes / 16; i += 32) z[i] = make_uint4(0, 0, 0, 0);
+              }
+              fence_proxy_async_smem();
+              __syncwarp();
+              if (lane == 0) mbar_arrive(mla ? &bar->k_full[st] : &bar->v_full[st]);
+            }
+          }
+        }
+      }
+    }
+  } else if (warp == C::MMA_WARP) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t fmt = BF16 ? 1u : 0u;
+      constexpr uint32_t idesc_qk = make_idesc_f16(fmt, 0, 0, BM, BN);
+      constexpr uint32_t idesc_pv = make_idesc_f16(fmt, 0, 1, BM, D);
+      constexpr uint32_t layout = swizzle_code(SWB);
+      const uint32_t sQa = smem_u32(sQ), sKa = smem_u32(sK), sVa = smem_u32(sV);
+      uint32_t q_full_ph = 0, p_ph[2] = {0, 0}, o_empty_ph[2] = {1, 1};
+      uint32_t fill = 0;
+
+      auto issue_s = [&](int t, int st) {
+        const uint32_t d = tmem_base + C::TM_S + t * BN;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t slab = (kk * 32) / SWB, inrow = (kk * 32) % SWB;
+          const uint64_t a = make_smem_desc(sQa + t * C::Q_BYTES + slab * (BM * SWB) + inrow, 16, 8 * SWB, layout);
+          const uint64_t b = make_smem_desc(sKa + st * C::KV_BYTES + slab * (BN * SWB) + inrow, 16, 8 * SWB, layout);
+          umma_ss(d, a, b, idesc_qk, kk > 0 ? 1u : 0u);
+        }
+      };
+      auto issue_pv = [&](int t, int st, bool acc) {
+        const uint32_t d = tmem_base + C::TM_O + t * D;
+        const uint32_t a_tm = tmem_base + C::TM_S + t * BN;  // P overwrites S (packed 16-bit pairs)
+        const uint32_t vbase = (mla ? sKa : sVa) + st * C::KV_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < BN / 16; ++kk) {
+          const uint64_t b = make_smem_desc(vbase + kk * 16 * SWB, BN * SWB, 8 * SWB, layout);
+          umma_ts(d, a_tm + kk * 8, b, idesc_pv, (acc || kk > 0) ? 1u : 0u);
+        }
+      };
+
+      for (int w = blockIdx.x; w < num_items && !failed; w += gridDim.x) {
+        const Item it = decode_item<C::PAIR, BN>(p, w);
+        const bool tv0 = it.qrows0 > 0, tv1 = NQ > 1 && it.qrows1 > 0;
+        const int nb = it.nblocks();
+        if (!mbar_wait(&bar->q_full, q_full_ph, abort_flag, tmo)) { fail(); break; }
+        q_full_ph ^= 1u;
+        {
+          const int st = fill % STAGES;
+          if (!mbar_wait(&bar->k_full[st], (fill / STAGES) & 1u, abort_flag, tmo)) { fail(); break; }
+          tc_fence_after();
+#pragma unroll
+          for (int t = 0; t < NQ; ++t)
+            if (t == 0 ? tv0 : tv1) { issue_s(t, st); umma_commit(&bar->s_full[t]); }
+          if (nb == 1) umma_commit(&bar->q_empty);
+        }
+        for (int j = 0; j < nb && !failed; ++j) {
+          const int st = (fill + j) % STAGES;
+          const int st1 = (fill + j + 1) % STAGES;
+          const uint32_t ph1 = ((fill + j + 1) / STAGES) & 1u;
+          if (!mla) {
+            if (!mbar_wait(&bar->v_full[st], ((fill + j) / STAGES) & 1u, abort_flag, tmo)) { fail(); break; }
+          }
+          bool k_next_ready = false;
+#pragma unroll
+          for (int t = 0; t < NQ; ++t) {
+            if (failed || !(t == 0 ? tv0 : tv1)) continue;
+            if (!mbar_wait(&bar->p_full[t], p_ph[t], abort_flag, tmo)) { fail(); continue; }
+            p_ph[t] ^= 1u;
+            if (j == 0) {
+              if (!mbar_wait(&bar->o_empty[t], o_empty_ph[t], abort_flag, tmo)) { fail(); continue; }
+              o_empty_ph[t] ^= 1u;
+            }
+            tc_fence_after();
+            issue_pv(t, st, j > 0);
+            if (j + 1 < nb) {
+              if (!k_next_ready) {
+                if (!mbar_wait(&bar->k_full[st1], ph1, abort_flag, tmo)) { fail(); continue; }
+                tc_fence_after();
+                k_next_ready = true;
+              }
+              issue_s(t, st1);
+              umma_commit(&bar->s_full[t]);
+            } else {
+              umma_commit(&bar->o_full[t]);
+            }
+          }
+          if (failed) break;
+          if (j + 2 == nb) umma_commit(&bar->q_empty);
+          umma_commit(&bar->kv_empty[st]);
+        }
+        fill += nb;
+      }
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ softmax + epilogue
+    const int t = warp >> 2;
+    const int wq = warp & 3;
+    const int row = wq * 32 + lane;
+    const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
+    const uint32_t tS = tmem_base + lane_off + C::TM_S + t * BN;
+    const uint32_t tO = tmem_base + lane_off + C::TM_O + t * D;
+    const float sl2 = p.scale_log2;
+    uint32_t s_ph = 0, o_ph = 0;
+    T* out = reinterpret_cast<T*>(p.out);
+
+    for (int w = blockIdx.x; w < num_items && !failed; w += gridDim.x) {
+      const Item it = decode_item<C::PAIR, BN>(p, w);
+      const int nrows = it.qrows(t);
+      if (nrows == 0) continue;
+      const bool row_valid = row < nrows;
+      float m = -INFINITY, l = 0.f;
+      const int nb = it.nblocks();
+      {
+        for (int j = 0; j < nb; ++j) {
+          int brow;
+          const Seg sgm = it.block_seg(j, BN, brow);
+          int kvv = min(BN, sgm.row1 - brow);
+          if (!row_valid) kvv = 0;
+          if (!mbar_wait(&bar->s_full[t], s_ph, abort_flag, tmo)) { fail(); }
+          failed = __any_sync(0xffffffffu, failed);
+          if (failed) break;
+          s_ph ^= 1u;
+          tc_fence_after();
+          uint32_t r[BN];
+          if constexpr (BN == 128) tmem_ld_x128(tS, r); else tmem_ld_x64(tS, r);
+          float mx = -INFINITY;
+#pragma unroll
+          for (int c = 0; c < BN; ++c) {
+            float x = __uint_as_float(r[c]) * sl2;
+            x = (c < kvv) ? x : -INFINITY;
+            r[c] = __float_as_uint(x);
+            mx = fmaxf(mx, x);
+          }
+          // Move the reference max only when this block raises it by more than 2^8.
+          bool need = false;
+          float alpha = 1.0f;
+          if (j == 0) {
+            m = mx;
+          } else if (mx > m + 8.0f) {
+            need = true;
+            alpha = ex2_approx(m - mx);
+            l *= alpha;
+            m = mx;
+          }
+          const float mu = (m == -INFINITY) ? 0.f : m;
+          float sum0 = 0.f, sum1 = 0.f;
+          uint32_t pk[BN / 2];
+#pragma unroll
+          for (int c = 0; c < BN / 2; ++c) {
+            const float p0 = ex2_approx(__uint_as_float(r[2 * c]) - mu);
+            const float p1 = ex2_approx(__uint_as_float(r[2 * c + 1]) - mu);
+            // The row sum uses the rounded P that the MMA multiplies, so O / l
+            // is an exact convex combination of V rows with those weights.
+            if constexpr (BF16) {
+              __nv_bfloat162 v2 = __floats2bfloat162_rn(p0, p1);
+              pk[c] = *reinterpret_cast<uint32_t*>(&v2);
+              sum0 += __uint_as_float(pk[c] << 16);
+              sum1 += __uint_as_float(pk[c] & 0xFFFF0000u);
+            } else {
+              __half2 v2 = __floats2half2_rn(p0, p1);
+              pk[c] = *reinterpret_cast<uint32_t*>(&v2);
+              const float2 f = __half22float2(v2);
+              sum0 += f.x;
+              sum1 += f.y;
+            }
+          }
+          l += sum0 + sum1;
+          if constexpr (BN == 128) tmem_st_x64(tS, pk); else tmem_st_x32(tS, pk);
+          if (__any_sync(0xffffffffu, need)) {
+            // PV of the previous block is complete (it was issued before this
+            // block's S), and PV of this block waits for p_full: O is stable.
+#pragma unroll
+            for (int c0 = 0; c0 < D; c0 += OC) {
+              uint32_t o[OC];
+              tmem_ld_chunk(tO + c0, o);
+#pragma unroll
+              for (int c = 0; c < OC; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
+              tmem_st_chunk(tO + c0, o);
+            }
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&bar->p_full[t]);
+        }
+        if (failed) break;
+      }
+      if (failed) break;
+      // epilogue: O / l  ->  global
+      if (!mbar_wait(&bar->o_full[t], o_ph, abort_flag, tmo)) fail();
+      failed = __any_sync(0xffffffffu, failed);
+      if (failed) break;
+      o_ph ^= 1u;
+      tc_fence_after();
+      const float inv = (l > 0.f) ? 1.0f / l : 1.0f;
+      T* orow = out + (it.out_row0 + t * BM + row) * (long long)D;
+#pragma unroll
+      for (int c0 = 0; c0 < D; c0 += OC) {
+        uint32_t o[OC];
+        tmem_ld_chunk(tO + c0, o);
+        if (row_valid) {
+          uint32_t v[OC / 2];
+#pragma unroll
+          for (int c = 0; c < OC / 2; ++c) {
+            const float a = __uint_as_float(o[2 * c]) * inv, b = __uint_as_float(o[2 * c + 1]) * inv;
+            if constexpr (BF16) {
+              __nv_bfloat162 v2 = __floats2bfloat162_rn(a, b);
+              v[c] = *reinterpret_cast<uint32_t*>(&v2);
+            } else {
+              __half2 v2 = __floats2half2_rn(a, b);
+              v[c] = *reinterpret_cast<uint32_t*>(&v2);
+            }
+          }
+          uint4* dst = reinterpret_cast<uint4*>(orow + c0);
+#pragma unroll
+          for (int q = 0; q < OC / 8; ++q) dst[q] = make_uint4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar->o_empty[t]);
+    }
+  }
+
+  // ------------------------------------------------------------ teardown
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == C::MMA_WARP) {
+    if (*abort_flag) {
+      // Give in-flight MMAs a bounded chance to retire before freeing TMEM.
+      const uint64_t t0 = global_timer_ns();
+      while (global_timer_ns() - t0 < 1000000ull) {}
+    }
+    tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+}
+
+}  // namespace fmlm

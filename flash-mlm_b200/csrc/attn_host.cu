@@ -1,0 +1,345 @@
+// C-ABI entry points for the attention forward path: argument validation,
+// TMA tensor-map encoding, the on-device tile scheduler and kernel dispatch.
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cmath>
+#include <mutex>
+
+#include "attn_fwd.cuh"
+#include "common.h"
+
+namespace fmlm {
+
+std::string& last_error_slot() {
+  static thread_local std::string s;
+  return s;
+}
+
+int device_sm_count() {
+  static int cache[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return 148;
+  if (cache[dev] == 0) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    cache[dev] = n > 0 ? n : 148;
+  }
+  return cache[dev];
+}
+
+namespace {
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// Encodes a 4-D tiled map {D, rows, heads, batch} over `v` with a box of
+// {swizzle_bytes / 2, box_rows, 1, 1} and the matching shared-memory swizzle.
+// Empty views get a 1-row map over `fallback` that the kernel never loads.
+int encode_view(CUtensorMap* m, const fmlm_view4& v, int D, int box_rows, int dtype, const void* fallback,
+                const char* name) {
+  auto enc = encode_fn();
+  if (!enc) return set_error(FMLM_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  const int swb = std::min(128, D * 2);
+  const bool empty = v.data == nullptr || v.rows <= 0 || v.heads <= 0 || v.batch <= 0;
+  const void* base = empty ? fallback : v.data;
+  if (!aligned16(base)) return set_error(FMLM_ERR_INVALID, "%s: base address must be 16-byte aligned", name);
+  cuuint64_t dims[4], strides[3];
+  dims[0] = static_cast<cuuint64_t>(D);
+  dims[1] = empty ? 1 : static_cast<cuuint64_t>(v.rows);
+  dims[2] = empty ? 1 : static_cast<cuuint64_t>(v.heads);
+  dims[3] = empty ? 1 : static_cast<cuuint64_t>(v.batch);
+  const int64_t rs = empty ? D : v.row_stride;
+  int64_t hs = empty ? D : v.head_stride;
+  int64_t bs = empty ? D : v.batch_stride;
+  if (!empty) {
+    if (rs < D || (rs * 2) % 16 != 0) return set_error(FMLM_ERR_INVALID, "%s: row stride must be >= head_dim and a multiple of 8 elements", name);
+    if (v.heads == 1 && (hs <= 0 || (hs * 2) % 16 != 0)) hs = rs * v.rows;
+    if (v.batch == 1 && (bs <= 0 || (bs * 2) % 16 != 0)) bs = hs * v.heads;
+    if ((hs * 2) % 16 != 0 || hs <= 0 || (bs * 2) % 16 != 0 || bs <= 0)
+      return set_error(FMLM_ERR_INVALID, "%s: head/batch strides must be positive multiples of 8 elements", name);
+  }
+  strides[0] = static_cast<cuuint64_t>(rs) * 2;
+  strides[1] = static_cast<cuuint64_t>(hs) * 2;
+  strides[2] = static_cast<cuuint64_t>(bs) * 2;
+  cuuint32_t box[4] = {static_cast<cuuint32_t>(swb / 2), static_cast<cuuint32_t>(box_rows), 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  const CUtensorMapSwizzle sw = swb == 128  ? CU_TENSOR_MAP_SWIZZLE_128B
+                                : swb == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                            : CU_TENSOR_MAP_SWIZZLE_32B;
+  const CUtensorMapDataType dt =
+      dtype == FMLM_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUresult r = enc(m, dt, 4, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(FMLM_ERR_CUDA, "%s: cuTensorMapEncodeTiled failed (%d)", name, (int)r);
+  return FMLM_OK;
+}
+
+// Builds the packed-mode work list: one entry per (sequence, query pair of
+// PAIR rows), sequences ordered by decreasing key count (longest first) so
+// the static round-robin over persistent CTAs balances.  Ties keep batch
+// order.  Single CTA; sorting is skipped above kSortMax sequences.
+constexpr int kSchedThreads = 1024;
+constexpr int kSortMax = 2048;
+
+__device__ __forceinline__ int seq_key_rows(const int* cu_q, const int* cu_kv, int b, int ctx_bs, int has_ctx,
+                                            int causal) {
+  const int L = cu_q[b + 1] - cu_q[b];
+  int kv = causal ? cu_q[b + 1] : L;
+  if (has_ctx) {
+    const int c = ctx_bs > 1 ? b : 0;
+    kv += cu_kv[c + 1] - cu_kv[c];
+  }
+  return kv;
+}
+
+__device__ int block_exclusive_scan(int v, int* warp_sums, int* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) warp_sums[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    const int nw = blockDim.x >> 5;
+    int s = lane < nw ? warp_sums[lane] : 0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, s, o);
+      if (lane >= o) s += y;
+    }
+    if (lane < nw) warp_sums[lane] = s;  // inclusive
+    if (lane == nw - 1) *total = s;
+  }
+  __syncthreads();
+  const int before = warp > 0 ? warp_sums[warp - 1] : 0;
+  const int r = before + x - v;
+  __syncthreads();
+  return r;
+}
+
+__global__ void __launch_bounds__(kSchedThreads) sched_kernel(const int* __restrict__ cu_q,
+                                                              const int* __restrict__ cu_kv, int B, int ctx_bs,
+                                                              int has_ctx, int causal, int pair, int* work,
+                                                              int cap) {
+  __shared__ int key[kSortMax];
+  __shared__ int order[kSortMax];
+  __shared__ int warp_sums[32];
+  __shared__ int total;
+  __shared__ int running;
+  const bool sort = B <= kSortMax;
+  if (threadIdx.x == 0) running = 0;
+  if (sort) {
+    for (int b = threadIdx.x; b < B; b += blockDim.x) key[b] = seq_key_rows(cu_q, cu_kv, b, ctx_bs, has_ctx, causal);
+    __syncthreads();
+    for (int b = threadIdx.x; b < B; b += blockDim.x) {
+      const int kb = key[b];
+      int r = 0;
+      for (int b2 = 0; b2 < B; ++b2) {
+        const int k2 = key[b2];
+        r += (k2 > kb) || (k2 == kb && b2 < b);
+      }
+      order[r] = b;
+    }
+  }
+  __syncthreads();
+  for (int base = 0; base < B; base += blockDim.x) {
+    const int s = base + threadIdx.x;
+    const int b = s < B ? (sort ? order[s] : s) : -1;
+    const int n = b >= 0 ? (cu_q[b + 1] - cu_q[b] + pair - 1) / pair : 0;
+    const int ex = block_exclusive_scan(n, warp_sums, &total);
+    const int off = running;
+    for (int i = 0; i < n; ++i) {
+      const int idx = off + ex + i;
+      if (idx < cap) work[1 + idx] = (b << 16) | i;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) running += total;
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) work[0] = running < cap ? running : cap;
+}
+
+int head_dim_supported(int d) { return d == 16 || d == 32 || d == 64 || d == 128 || d == 256; }
+int pair_rows(int d) { return d >= 256 ? 128 : 256; }
+
+template <int D, int NQ, bool BF16>
+int launch_attn(const CUtensorMap* m, const AttnParams& p, int grid, cudaStream_t s) {
+  using C = AttnCfg<D, NQ>;
+  auto kern = attn_fwd_kernel<D, NQ, BF16>;
+  // At least 116 KB so that exactly one CTA (and one TMEM owner) lives per SM.
+  const int smem = std::max(C::SMEM_BYTES, 116 * 1024);
+  static bool configured[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !configured[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return set_error(FMLM_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+    configured[dev] = true;
+  }
+  kern<<<grid, C::THREADS, smem, s>>>(m[0], m[1], m[2], m[3], m[4], p);
+  return check_launch("attn_fwd_kernel");
+}
+
+template <bool BF16>
+int dispatch(int D, const CUtensorMap* m, const AttnParams& p, int grid, cudaStream_t s) {
+  switch (D) {
+    case 16: return launch_attn<16, 2, BF16>(m, p, grid, s);
+    case 32: return launch_attn<32, 2, BF16>(m, p, grid, s);
+    case 64: return launch_attn<64, 2, BF16>(m, p, grid, s);
+    case 128: return launch_attn<128, 2, BF16>(m, p, grid, s);
+    case 256: return launch_attn<256, 1, BF16>(m, p, grid, s);
+    default: return set_error(FMLM_ERR_UNSUPPORTED, "head_dim %d is not supported", D);
+  }
+}
+
+int kv_box_rows(int D) { return D >= 256 ? 64 : 128; }
+
+constexpr unsigned long long kTimeoutNs = 2000000000ull;  // 2 s per wait
+
+int check_common(int dtype, int D, const void* out) {
+  if (dtype != FMLM_DTYPE_F16 && dtype != FMLM_DTYPE_BF16) return set_error(FMLM_ERR_INVALID, "dtype must be f16 or bf16");
+  if (!head_dim_supported(D)) return set_error(FMLM_ERR_UNSUPPORTED, "HEAD_DIM must be one of {16, 32, 64, 128, 256}");
+  if (!out || !aligned16(out)) return set_error(FMLM_ERR_INVALID, "out must be a 16-byte aligned device pointer");
+  return FMLM_OK;
+}
+
+}  // namespace
+}  // namespace fmlm
+
+using namespace fmlm;
+
+extern "C" int fmlm_attn_dense_fwd(const fmlm_dense_args* a, void* stream) {
+  if (!a) return set_error(FMLM_ERR_INVALID, "null args");
+  int rc = check_common(a->dtype, a->head_dim, a->out);
+  if (rc) return rc;
+  const int D = a->head_dim;
+  if (a->batch <= 0 || a->num_heads <= 0 || a->seq_len < 0) return set_error(FMLM_ERR_INVALID, "bad B/H/N");
+  if (a->seq_len == 0) return FMLM_OK;
+  const bool has_ctx = !a->prefill && a->context_len > 0;
+  if (has_ctx && a->context_batch_size > 1 && a->context_batch_size < a->batch)
+    return set_error(FMLM_ERR_INVALID, "context_batch_size (%d) must be 1 or >= batch (%d)", a->context_batch_size, a->batch);
+  CUtensorMap m[5];
+  const int kb = kv_box_rows(D);
+  if ((rc = encode_view(&m[0], a->q, D, 128, a->dtype, a->q.data, "q"))) return rc;
+  if ((rc = encode_view(&m[1], a->k, D, kb, a->dtype, a->q.data, "k"))) return rc;
+  if ((rc = encode_view(&m[2], a->is_mla ? a->k : a->v, D, kb, a->dtype, a->q.data, "v"))) return rc;
+  fmlm_view4 empty = {nullptr, 0, 0, 0, 0, 0, 0};
+  if ((rc = encode_view(&m[3], has_ctx ? a->k_cache : empty, D, kb, a->dtype, a->q.data, "k_cache"))) return rc;
+  if ((rc = encode_view(&m[4], has_ctx ? (a->is_mla ? a->k_cache : a->v_cache) : empty, D, kb, a->dtype, a->q.data,
+                        "v_cache")))
+    return rc;
+  AttnParams p{};
+  p.mode = 0;
+  p.has_ctx = has_ctx;
+  p.is_mla = a->is_mla;
+  p.B = a->batch; p.H = a->num_heads; p.N = a->seq_len;
+  p.ctx_bs = a->context_batch_size;
+  p.ctx_len = a->context_len;
+  const int pr = pair_rows(D);
+  const long long items = (long long)a->batch * a->num_heads * ((a->seq_len + pr - 1) / pr);
+  if (items > 0x7fffffffLL) return set_error(FMLM_ERR_INVALID, "problem too large");
+  p.num_items = (int)items;
+  p.scale_log2 = a->scale * 1.4426950408889634f;
+  p.out = a->out;
+  static int dummy_err_host = 0;
+  (void)dummy_err_host;
+  if (!a->error_word) return set_error(FMLM_ERR_INVALID, "error_word is required");
+  p.err = a->error_word;
+  p.timeout_ns = kTimeoutNs;
+  const int grid = (int)std::min<long long>(items, device_sm_count());
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  return a->dtype == FMLM_DTYPE_BF16 ? dispatch<true>(D, m, p, grid, s) : dispatch<false>(D, m, p, grid, s);
+}
+
+extern "C" size_t fmlm_packed_workspace_bytes(int32_t batch, int64_t total_q_len, int32_t head_dim) {
+  const int64_t pr = head_dim >= 256 ? 128 : 256;
+  const int64_t cap = total_q_len / pr + batch + 2;
+  return (size_t)((cap + 2) * sizeof(int32_t) + 15) / 16 * 16;
+}
+
+extern "C" int fmlm_attn_packed_fwd(const fmlm_packed_args* a, void* stream) {
+  if (!a) return set_error(FMLM_ERR_INVALID, "null args");
+  int rc = check_common(a->dtype, a->head_dim, a->out);
+  if (rc) return rc;
+  const int D = a->head_dim;
+  if (a->batch <= 0 || a->num_heads <= 0) return set_error(FMLM_ERR_INVALID, "bad batch / num_heads");
+  if (a->batch >= 32768) return set_error(FMLM_ERR_INVALID, "batch must be < 32768");
+  if (!a->cu_seqlens_q) return set_error(FMLM_ERR_INVALID, "cu_seqlens_q is required");
+  if (!a->error_word) return set_error(FMLM_ERR_INVALID, "error_word is required");
+  const bool q_padded = a->q_layout == FMLM_LAYOUT_PADDED;
+  const bool kv_padded = a->kv_layout == FMLM_LAYOUT_PADDED;
+  if (kv_padded && a->causal_query_seq_attn)
+    return set_error(FMLM_ERR_INVALID, "causal_query_seq_attn needs packed main k/v");
+  if ((q_padded || kv_padded) && a->seq_len <= 0) return set_error(FMLM_ERR_INVALID, "seq_len required for padded layouts");
+  if ((int64_t)a->seq_len > 65535LL * pair_rows(D)) return set_error(FMLM_ERR_INVALID, "sequence too long");
+  const bool has_ctx = !a->prefill && a->cu_seqlens_kv != nullptr && a->k_cache.data != nullptr &&
+                       a->k_cache.rows > 0;
+  if (has_ctx && a->context_batch_size > 1 && a->context_batch_size < a->batch)
+    return set_error(FMLM_ERR_INVALID, "context_batch_size (%d) must be 1 or >= batch (%d)", a->context_batch_size, a->batch);
+  const size_t need = fmlm_packed_workspace_bytes(a->batch, a->total_q_len, D);
+  if (!a->workspace || a->workspace_bytes < need || !aligned16(a->workspace))
+    return set_error(FMLM_ERR_INVALID, "workspace too small (%zu bytes needed)", need);
+
+  CUtensorMap m[5];
+  const int kb = kv_box_rows(D);
+  if ((rc = encode_view(&m[0], a->q, D, 128, a->dtype, a->q.data, "q"))) return rc;
+  if ((rc = encode_view(&m[1], a->k, D, kb, a->dtype, a->q.data, "k"))) return rc;
+  if ((rc = encode_view(&m[2], a->is_mla ? a->k : a->v, D, kb, a->dtype, a->q.data, "v"))) return rc;
+  fmlm_view4 empty = {nullptr, 0, 0, 0, 0, 0, 0};
+  if ((rc = encode_view(&m[3], has_ctx ? a->k_cache : empty, D, kb, a->dtype, a->q.data, "k_cache"))) return rc;
+  if ((rc = encode_view(&m[4], has_ctx ? (a->is_mla ? a->k_cache : a->v_cache) : empty, D, kb, a->dtype, a->q.data,
+                        "v_cache")))
+    return rc;
+
+  const int pr = pair_rows(D);
+  const int64_t cap = a->total_q_len / pr + a->batch + 2;
+  int* work = reinterpret_cast<int*>(a->workspace);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (!a->reuse_schedule) {
+    sched_kernel<<<1, kSchedThreads, 0, s>>>(a->cu_seqlens_q, has_ctx ? a->cu_seqlens_kv : a->cu_seqlens_q,
+                                             a->batch, a->context_batch_size, has_ctx, a->causal_query_seq_attn, pr,
+                                             work, (int)cap);
+    if ((rc = check_launch("sched_kernel"))) return rc;
+  }
+
+  AttnParams p{};
+  p.mode = 1;
+  p.q_padded = q_padded;
+  p.main_padded = kv_padded;
+  p.causal = a->causal_query_seq_attn;
+  p.has_ctx = has_ctx;
+  p.is_mla = a->is_mla;
+  p.B = a->batch; p.H = a->num_heads; p.N = a->seq_len;
+  p.ctx_bs = a->context_batch_size;
+  p.t_out = a->out_rows_per_head;
+  p.scale_log2 = a->scale * 1.4426950408889634f;
+  p.cu_q = a->cu_seqlens_q;
+  p.cu_kv = has_ctx ? a->cu_seqlens_kv : a->cu_seqlens_q;
+  p.work = work;
+  p.out = a->out;
+  p.err = a->error_word;
+  p.timeout_ns = kTimeoutNs;
+  const long long items_bound = cap * (long long)a->num_heads;
+  const int grid = (int)std::min<long long>(items_bound, device_sm_count());
+  return a->dtype == FMLM_DTYPE_BF16 ? dispatch<true>(D, m, p, grid, s) : dispatch<false>(D, m, p, grid, s);
+}
+
+extern "C" const char* fmlm_last_error(void) { return last_error_slot().c_str(); }
+
+extern "C" int fmlm_version(void) { return 100; }

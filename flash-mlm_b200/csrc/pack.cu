@@ -1,0 +1,301 @@
+// Pack metadata, pack (gather + pad), unpack (scatter + zero) and pad kernels.
+//
+// These restate the torch index arithmetic of the reference host utilities
+// (src/flash_mlm/host/host_utils.py) as single-pass vectorised CUDA kernels:
+//   build_pack_metadata / _build_query_tile_map_from_cu_seqlens  :27-107
+//   pack_for_kernel / _pack_flatten_for_kernel_into              :266-289, :397-420
+//   pad_packed_main_tensors_for_mlm_compressed                   :494-584
+//   unpack_from_kernel                                           :587-615
+// Copies move the widest naturally aligned unit (16/8/4/2/1 bytes) that the
+// row size, pointers and strides allow, so every access is coalesced.
+#include <algorithm>
+
+#include "common.h"
+
+namespace fmlm {
+namespace {
+
+constexpr int kScanThreads = 1024;
+
+__device__ int block_scan_excl(int v, int* warp_sums, int* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) warp_sums[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    const int nw = blockDim.x >> 5;
+    int s = lane < nw ? warp_sums[lane] : 0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, s, o);
+      if (lane >= o) s += y;
+    }
+    if (lane < nw) warp_sums[lane] = s;
+    if (lane == nw - 1) *total = s;
+  }
+  __syncthreads();
+  const int r = (warp > 0 ? warp_sums[warp - 1] : 0) + x - v;
+  __syncthreads();
+  return r;
+}
+
+// counters: [0] total tokens, [1] total tiles, [2] error, [3 .. 3+B] tile prefix.
+__global__ void __launch_bounds__(kScanThreads) meta_scan_kernel(const int* __restrict__ lengths, int B, int N,
+                                                                 int block_n, int* __restrict__ cu,
+                                                                 int* __restrict__ counters) {
+  __shared__ int ws[32];
+  __shared__ int tot_l, tot_t, run_l, run_t;
+  if (threadIdx.x == 0) { run_l = 0; run_t = 0; cu[0] = 0; }
+  int bad = 0;
+  for (int base = 0; base < B; base += blockDim.x) {
+    const int b = base + threadIdx.x;
+    const int L = b < B ? lengths[b] : 0;
+    if (b < B && (L < 0 || L > N)) bad = 1;
+    const int Lc = (L < 0) ? 0 : L;
+    const int tiles = (Lc + block_n - 1) / block_n;
+    __syncthreads();
+    const int rl = run_l, rt = run_t;
+    const int el = block_scan_excl(L, ws, &tot_l);
+    const int et = block_scan_excl(tiles, ws, &tot_t);
+    if (b < B) {
+      cu[b + 1] = rl + el + L;
+      counters[3 + b] = rt + et;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) { run_l += tot_l; run_t += tot_t; }
+  }
+  bad = __syncthreads_or(bad);
+  if (threadIdx.x == 0) {
+    counters[0] = run_l;
+    counters[1] = run_t;
+    counters[2] = bad;
+    counters[3 + B] = run_t;
+  }
+}
+
+// One CTA per sequence: token indices b*N+t of its valid tokens and its query tiles.
+__global__ void meta_fill_kernel(const int* __restrict__ cu, const int* __restrict__ counters, int N, int block_n,
+                                 long long* __restrict__ token_indices, int* __restrict__ batch_ids,
+                                 int* __restrict__ tile_starts) {
+  const int b = blockIdx.x;
+  if (counters[2]) return;
+  const int s = cu[b], L = cu[b + 1] - s;
+  const int base = b * N;  // int32 product, as the reference builds it
+  if (token_indices)
+    for (int t = threadIdx.x; t < L; t += blockDim.x) token_indices[s + t] = (long long)(base + t);
+  const int tp = counters[3 + b];
+  const int nt = (L + block_n - 1) / block_n;
+  for (int i = threadIdx.x; i < nt; i += blockDim.x) {
+    batch_ids[tp + i] = b;
+    tile_starts[tp + i] = s + i * block_n;
+  }
+}
+
+template <int V>
+struct VecT;
+template <> struct VecT<16> { using T = uint4; };
+template <> struct VecT<8> { using T = uint2; };
+template <> struct VecT<4> { using T = uint32_t; };
+template <> struct VecT<2> { using T = uint16_t; };
+template <> struct VecT<1> { using T = uint8_t; };
+
+__device__ __forceinline__ int find_seq(const int* __restrict__ cu, int B, long long r) {
+  int lo = 0, hi = B - 1;  // largest b with cu[b] <= r
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (cu[mid] <= r) lo = mid; else hi = mid - 1;
+  }
+  return lo;
+}
+
+// out[h][r] = x[b(r)][h][r - cu[b(r)]] for r < total_tokens, zero for r < total_padded.
+template <int V>
+__global__ void pack_rows_kernel(const uint8_t* __restrict__ x, long long sb, long long sh, long long sr,
+                                 int row_bytes, int H, const int* __restrict__ cu, int B, long long total_tokens,
+                                 long long total_padded, uint8_t* __restrict__ out) {
+  using T = typename VecT<V>::T;
+  const int nvec = row_bytes / V;
+  const long long n = (long long)H * total_padded * nvec;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const long long row = i / nvec;
+    const int v = (int)(i - row * nvec);
+    const int h = (int)(row / total_padded);
+    const long long r = row - (long long)h * total_padded;
+    T val{};
+    if (r < total_tokens) {
+      const int b = find_seq(cu, B, r);
+      const long long t = r - cu[b];
+      val = *reinterpret_cast<const T*>(x + b * sb + h * sh + t * sr + (long long)v * V);
+    }
+    *reinterpret_cast<T*>(out + row * row_bytes + (long long)v * V) = val;
+  }
+}
+
+// out[b][h][n] = packed[h][cu[b] + n] for n < len(b), zero otherwise.
+template <int V>
+__global__ void unpack_rows_kernel(const uint8_t* __restrict__ packed, long long total_tokens, int H, int row_bytes,
+                                   const int* __restrict__ cu, int B, int N, uint8_t* __restrict__ out) {
+  using T = typename VecT<V>::T;
+  const int nvec = row_bytes / V;
+  const long long n = (long long)B * H * N * nvec;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const long long row = i / nvec;
+    const int v = (int)(i - row * nvec);
+    const int t = (int)(row % N);
+    const long long bh = row / N;
+    const int h = (int)(bh % H);
+    const int b = (int)(bh / H);
+    const int s = cu[b];
+    T val{};
+    if (t < cu[b + 1] - s)
+      val = *reinterpret_cast<const T*>(packed + ((long long)h * total_tokens + s + t) * row_bytes + (long long)v * V);
+    *reinterpret_cast<T*>(out + row * row_bytes + (long long)v * V) = val;
+  }
+}
+
+// dst[h][r] = src[h][r] for r < old_len, zero for r < new_len.
+template <int V>
+__global__ void pad_rows_kernel(const uint8_t* __restrict__ src, long long old_len, long long new_len, int heads,
+                                int row_bytes, uint8_t* __restrict__ dst) {
+  using T = typename VecT<V>::T;
+  const int nvec = row_bytes / V;
+  const long long n = (long long)heads * new_len * nvec;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const long long row = i / nvec;
+    const int v = (int)(i - row * nvec);
+    const long long h = row / new_len;
+    const long long r = row - h * new_len;
+    T val{};
+    if (r < old_len) val = *reinterpret_cast<const T*>(src + (h * old_len + r) * row_bytes + (long long)v * V);
+    *reinterpret_cast<T*>(dst + row * row_bytes + (long long)v * V) = val;
+  }
+}
+
+int pick_vec(long long a) {
+  for (int v = 16; v > 1; v >>= 1)
+    if (a % v == 0) return v;
+  return 1;
+}
+
+int grid_for(long long n) {
+  const long long blocks = (n + 255) / 256;
+  return (int)std::max<long long>(1, std::min<long long>(blocks, (long long)device_sm_count() * 16));
+}
+
+}  // namespace
+}  // namespace fmlm
+
+using namespace fmlm;
+
+extern "C" int fmlm_build_pack_metadata(const int32_t* lengths, int32_t B, int32_t N, int32_t block_n,
+                                        int32_t* cu_seqlens, int64_t* token_indices, int32_t* batch_ids_q,
+                                        int32_t* q_tile_starts_q, int32_t* counters, void* stream) {
+  if (B < 0 || N < 0) return set_error(FMLM_ERR_INVALID, "N must be >= 0");
+  if (block_n < 1) return set_error(FMLM_ERR_INVALID, "block_n must be >= 1");
+  if (!cu_seqlens || !counters || (B > 0 && (!lengths || !batch_ids_q || !q_tile_starts_q)))
+    return set_error(FMLM_ERR_INVALID, "null pointer argument");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  meta_scan_kernel<<<1, kScanThreads, 0, s>>>(lengths, B, N, block_n, cu_seqlens, counters);
+  int rc = check_launch("meta_scan_kernel");
+  if (rc || B == 0) return rc;
+  meta_fill_kernel<<<B, 256, 0, s>>>(cu_seqlens, counters, N, block_n, reinterpret_cast<long long*>(token_indices),
+                                     batch_ids_q, q_tile_starts_q);
+  return check_launch("meta_fill_kernel");
+}
+
+extern "C" int fmlm_pack_rows(const fmlm_view4* x, int32_t elem_bytes, int32_t head_dim, const int32_t* cu_seqlens,
+                              int32_t B, int64_t total_tokens, int64_t total_padded, void* out, void* stream) {
+  if (!x || !out || !cu_seqlens) return set_error(FMLM_ERR_INVALID, "null pointer argument");
+  if (elem_bytes <= 0 || head_dim <= 0 || B <= 0 || total_tokens < 0 || total_padded < total_tokens)
+    return set_error(FMLM_ERR_INVALID, "bad pack sizes");
+  const int H = (int)x->heads;
+  const long long row_bytes = (long long)elem_bytes * head_dim;
+  const long long n_rows = (long long)H * total_padded;
+  if (n_rows == 0) return FMLM_OK;
+  if (total_tokens > 0 && !x->data) return set_error(FMLM_ERR_INVALID, "x has no data");
+  const long long sb = x->batch_stride * elem_bytes, sh = x->head_stride * elem_bytes, sr = x->row_stride * elem_bytes;
+  long long g = row_bytes;
+  for (long long a : {sb, sh, sr, (long long)reinterpret_cast<uintptr_t>(x->data),
+                      (long long)reinterpret_cast<uintptr_t>(out)})
+    g = std::__gcd(g, a == 0 ? g : a);
+  const int V = pick_vec(g);
+  const long long n = n_rows * (row_bytes / V);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  auto px = reinterpret_cast<const uint8_t*>(x->data);
+  auto po = reinterpret_cast<uint8_t*>(out);
+#define FMLM_PACK(VV)                                                                                            \
+  pack_rows_kernel<VV><<<grid_for(n), 256, 0, s>>>(px, sb, sh, sr, (int)row_bytes, H, cu_seqlens, B, total_tokens, \
+                                                   total_padded, po)
+  switch (V) {
+    case 16: FMLM_PACK(16); break;
+    case 8: FMLM_PACK(8); break;
+    case 4: FMLM_PACK(4); break;
+    case 2: FMLM_PACK(2); break;
+    default: FMLM_PACK(1); break;
+  }
+#undef FMLM_PACK
+  return check_launch("pack_rows_kernel");
+}
+
+extern "C" int fmlm_unpack_rows(const void* packed, int64_t total_tokens, int32_t H, int32_t head_dim,
+                                int32_t elem_bytes, const int32_t* cu_seqlens, int32_t B, int32_t N, void* out,
+                                void* stream) {
+  if (!out || !cu_seqlens) return set_error(FMLM_ERR_INVALID, "null pointer argument");
+  if (elem_bytes <= 0 || head_dim <= 0 || H < 0 || B < 0 || N < 0 || total_tokens < 0)
+    return set_error(FMLM_ERR_INVALID, "bad unpack sizes");
+  const long long row_bytes = (long long)elem_bytes * head_dim;
+  const long long n_rows = (long long)B * H * N;
+  if (n_rows == 0) return FMLM_OK;
+  long long g = row_bytes;
+  for (long long a : {(long long)reinterpret_cast<uintptr_t>(packed), (long long)reinterpret_cast<uintptr_t>(out)})
+    g = std::__gcd(g, a == 0 ? g : a);
+  const int V = pick_vec(g);
+  const long long n = n_rows * (row_bytes / V);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  auto pp = reinterpret_cast<const uint8_t*>(packed);
+  auto po = reinterpret_cast<uint8_t*>(out);
+#define FMLM_UNPACK(VV) \
+  unpack_rows_kernel<VV><<<grid_for(n), 256, 0, s>>>(pp, total_tokens, H, (int)row_bytes, cu_seqlens, B, N, po)
+  switch (V) {
+    case 16: FMLM_UNPACK(16); break;
+    case 8: FMLM_UNPACK(8); break;
+    case 4: FMLM_UNPACK(4); break;
+    case 2: FMLM_UNPACK(2); break;
+    default: FMLM_UNPACK(1); break;
+  }
+#undef FMLM_UNPACK
+  return check_launch("unpack_rows_kernel");
+}
+
+extern "C" int fmlm_pad_packed_rows(const void* src, int64_t old_len, int64_t new_len, int32_t heads,
+                                    int32_t head_dim, int32_t elem_bytes, void* dst, void* stream) {
+  if (!dst || (!src && old_len > 0)) return set_error(FMLM_ERR_INVALID, "null pointer argument");
+  if (old_len < 0 || new_len < old_len || heads < 0 || head_dim <= 0 || elem_bytes <= 0)
+    return set_error(FMLM_ERR_INVALID, "bad pad sizes");
+  const long long row_bytes = (long long)elem_bytes * head_dim;
+  const long long n_rows = (long long)heads * new_len;
+  if (n_rows == 0) return FMLM_OK;
+  long long g = row_bytes;
+  for (long long a : {(long long)reinterpret_cast<uintptr_t>(src), (long long)reinterpret_cast<uintptr_t>(dst)})
+    g = std::__gcd(g, a == 0 ? g : a);
+  const int V = pick_vec(g);
+  const long long n = n_rows * (row_bytes / V);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  auto ps = reinterpret_cast<const uint8_t*>(src);
+  auto pd = reinterpret_cast<uint8_t*>(dst);
+#define FMLM_PAD(VV) pad_rows_kernel<VV><<<grid_for(n), 256, 0, s>>>(ps, old_len, new_len, heads, (int)row_bytes, pd)
+  switch (V) {
+    case 16: FMLM_PAD(16); break;
+    case 8: FMLM_PAD(8); break;
+    case 4: FMLM_PAD(4); break;
+    case 2: FMLM_PAD(2); break;
+    default: FMLM_PAD(1); break;
+  }
+#undef FMLM_PAD
+  return check_launch("pad_rows_kernel");
+}
