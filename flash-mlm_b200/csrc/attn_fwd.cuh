@@ -422,6 +422,8 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
     const uint32_t tS = tmem_base + lane_off + C::TM_S + t * BN;
     const uint32_t tO = tmem_base + lane_off + C::TM_O + t * D;
     const float sl2 = p.scale_log2;
+    const bool pos_scale = sl2 > 0.f;
+    const float fac = pos_scale ? sl2 : 1.0f;
     uint32_t s_ph = 0, o_ph = 0;
     T* out = reinterpret_cast<T*>(p.out);
 
@@ -445,13 +447,27 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
           tc_fence_after();
           uint32_t r[BN];
           if constexpr (BN == 128) tmem_ld_x128(tS, r); else tmem_ld_x64(tS, r);
-          float mx = -INFINITY;
+          // With a positive scale the row max is taken on raw scores and the
+          // scale is folded into the exp2 argument (one FFMA per element);
+          // otherwise scores are scaled first.
+          if (!pos_scale) {
 #pragma unroll
-          for (int c = 0; c < BN; ++c) {
-            float x = __uint_as_float(r[c]) * sl2;
-            x = (c < kvv) ? x : -INFINITY;
-            r[c] = __float_as_uint(x);
-            mx = fmaxf(mx, x);
+            for (int c = 0; c < BN; ++c) r[c] = __float_as_uint(__uint_as_float(r[c]) * sl2);
+          }
+          if (kvv < BN) {
+#pragma unroll
+            for (int c = 0; c < BN; ++c)
+              if (c >= kvv) r[c] = 0xff800000u;  // -inf
+          }
+          float mx;
+          {
+            float m8[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) m8[i] = __uint_as_float(r[i]);
+#pragma unroll
+            for (int c = 8; c < BN; ++c) m8[c & 7] = fmaxf(m8[c & 7], __uint_as_float(r[c]));
+            mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])), fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
+            mx *= fac;  // -inf stays -inf (fac > 0)
           }
           // Move the reference max only when this block raises it by more than 2^8.
           bool need = false;
@@ -464,29 +480,29 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
             l *= alpha;
             m = mx;
           }
-          const float mu = (m == -INFINITY) ? 0.f : m;
-          float sum0 = 0.f, sum1 = 0.f;
+          const float neg_mu = (m == -INFINITY) ? 0.f : -m;
+          float sums[4] = {0.f, 0.f, 0.f, 0.f};
           uint32_t pk[BN / 2];
 #pragma unroll
           for (int c = 0; c < BN / 2; ++c) {
-            const float p0 = ex2_approx(__uint_as_float(r[2 * c]) - mu);
-            const float p1 = ex2_approx(__uint_as_float(r[2 * c + 1]) - mu);
+            const float p0 = ex2_approx(fmaf(__uint_as_float(r[2 * c]), fac, neg_mu));
+            const float p1 = ex2_approx(fmaf(__uint_as_float(r[2 * c + 1]), fac, neg_mu));
             // The row sum uses the rounded P that the MMA multiplies, so O / l
             // is an exact convex combination of V rows with those weights.
             if constexpr (BF16) {
               __nv_bfloat162 v2 = __floats2bfloat162_rn(p0, p1);
               pk[c] = *reinterpret_cast<uint32_t*>(&v2);
-              sum0 += __uint_as_float(pk[c] << 16);
-              sum1 += __uint_as_float(pk[c] & 0xFFFF0000u);
+              sums[(2 * c) & 3] += __uint_as_float(pk[c] << 16);
+              sums[(2 * c + 1) & 3] += __uint_as_float(pk[c] & 0xFFFF0000u);
             } else {
               __half2 v2 = __floats2half2_rn(p0, p1);
               pk[c] = *reinterpret_cast<uint32_t*>(&v2);
               const float2 f = __half22float2(v2);
-              sum0 += f.x;
-              sum1 += f.y;
+              sums[(2 * c) & 3] += f.x;
+              sums[(2 * c + 1) & 3] += f.y;
             }
           }
-          l += sum0 + sum1;
+          l += (sums[0] + sums[1]) + (sums[2] + sums[3]);
           if constexpr (BN == 128) tmem_st_x64(tS, pk); else tmem_st_x32(tS, pk);
           if (__any_sync(0xffffffffu, need)) {
             // PV of the previous block is complete (it was issued before this

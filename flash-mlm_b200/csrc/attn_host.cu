@@ -257,8 +257,6 @@ extern "C" int fmlm_attn_dense_fwd(const fmlm_dense_args* a, void* stream) {
   p.num_items = (int)items;
   p.scale_log2 = a->scale * 1.4426950408889634f;
   p.out = a->out;
-  static int dummy_err_host = 0;
-  (void)dummy_err_host;
   if (!a->error_word) return set_error(FMLM_ERR_INVALID, "error_word is required");
   p.err = a->error_word;
   p.timeout_ns = kTimeoutNs;

@@ -52,15 +52,19 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar_addr, uint32_t parity
 
 // Waits until the phase with the given parity has completed.  Gives up when
 // `abort_flag` (shared memory) becomes non-zero or after `limit_ns`; returns
-// false in that case.
+// false in that case.  The timer is only consulted after a few thousand
+// unsuccessful polls, so a wait that completes normally costs only try_waits.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
                                           uint64_t limit_ns) {
   const uint32_t a = smem_u32(bar);
-  if (mbar_try_wait(a, parity)) return true;
+#pragma unroll 1
+  for (int i = 0; i < 4096; ++i)
+    if (mbar_try_wait(a, parity)) return true;
   const uint64_t t0 = global_timer_ns();
+#pragma unroll 1
   for (uint32_t it = 1;; ++it) {
     if (mbar_try_wait(a, parity)) return true;
-    if ((it & 63u) == 0u) {
+    if ((it & 255u) == 0u) {
       if (*abort_flag) return false;
       if (global_timer_ns() - t0 > limit_ns) return false;
     }
