@@ -52,7 +52,25 @@ struct AttnParams {
   void* out;        // [rows, D]
   int* err;         // device error word
   unsigned long long timeout_ns;
+  unsigned long long* trace;  // optional timeline buffer (builds with FMLM_TRACE only)
 };
+
+// Opt-in timeline instrumentation (builds with -DFMLM_TRACE only): in CTA 0
+// each recording thread (one per role) appends (event << 48 | clock) records
+// to its own shared-memory slice; the slices are copied to p.trace at exit
+// (p.trace[0..3] = record counts, role r's records from 4 + r * kTraceSlots).
+#ifdef FMLM_TRACE
+constexpr int kTraceSlots = 1024;
+#define FMLM_TR(ev)                                                                                   \
+  do {                                                                                                \
+    if (tr_role >= 0 && tr_n < kTraceSlots)                                                           \
+      tr_buf[tr_role * kTraceSlots + tr_n++] = ((unsigned long long)(ev) << 48) | (clock64() & 0xFFFFFFFFFFFFull); \
+  } while (0)
+#else
+#define FMLM_TR(ev) \
+  do {              \
+  } while (0)
+#endif
 
 template <int D_, int NQ_>
 struct AttnCfg {
@@ -69,12 +87,21 @@ struct AttnCfg {
   static constexpr int STAGES = (D <= 32) ? 4 : (D <= 64) ? 3 : 2;
   static constexpr int NUM_SOFTMAX_WARPS = 4 * NQ;
   static constexpr int TMA_WARP = NUM_SOFTMAX_WARPS;
-  static constexpr int MMA_WARP = NUM_SOFTMAX_WARPS + 1;
-  static constexpr int THREADS = 32 * (NUM_SOFTMAX_WARPS + 2);
-  static constexpr int MAX_REGS = (65536 / THREADS) / 8 * 8 > 255 ? 255 : (65536 / THREADS) / 8 * 8;
+  static constexpr int MMA_WARP = NUM_SOFTMAX_WARPS + 1;  // one MMA-issuing warp per tile: MMA_WARP + t
+  static constexpr int THREADS = 32 * (NUM_SOFTMAX_WARPS + 1 + NQ);
+  // Each SM sub-partition owns a quarter of the register file and every
+  // fourth warp of the CTA, so the budget is 16384 / (32 * ceil(warps / 4)).
+  static constexpr int WARPS_PER_SMSP = (NUM_SOFTMAX_WARPS + 1 + NQ + 3) / 4;
+  static constexpr int MAX_REGS = (16384 / (32 * WARPS_PER_SMSP)) / 8 * 8 > 255 ? 255
+                                : (16384 / (32 * WARPS_PER_SMSP)) / 8 * 8;
+  // P gets its own TMEM columns when they fit (D <= 64 with two tiles, or one
+  // tile): S_t(j+1) can then be issued as soon as the softmax has read S_t(j).
+  // Otherwise P is written over the first BN/2 columns of S_t.
+  static constexpr bool SEP_P = NQ * (BN + D + BN / 2) <= 512;
   static constexpr int TM_S = 0;                   // S_t at column t*BN
   static constexpr int TM_O = NQ * BN;             // O_t at column TM_O + t*D
-  static constexpr int TMEM_USED = NQ * (BN + D);
+  static constexpr int TM_P = SEP_P ? NQ * (BN + D) : 0;  // P_t at TM_P + t*BN/2 (or over S_t)
+  static constexpr int TMEM_USED = NQ * (BN + D) + (SEP_P ? NQ * BN / 2 : 0);
   static constexpr int TMEM_COLS = TMEM_USED <= 32 ? 32 : TMEM_USED <= 64 ? 64 : TMEM_USED <= 128 ? 128
                                  : TMEM_USED <= 256 ? 256 : 512;
   static_assert(TMEM_USED <= 512, "TMEM budget");
@@ -173,6 +200,7 @@ struct __align__(8) AttnBarriers {
   uint64_t q_full, q_empty, fix;
   uint64_t k_full[4], v_full[4], kv_empty[4];
   uint64_t s_full[2], p_full[2], o_full[2], o_empty[2];
+  uint64_t s_free[2], pv_done[2];  // separate-P pipeline only
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -204,21 +232,35 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const bool mla = p.is_mla != 0;
+#ifdef FMLM_TRACE
+  __shared__ unsigned long long tr_buf[4 * kTraceSlots];
+  __shared__ int tr_cnt[4];
+  int tr_n = 0;
+  int tr_role = -1;
+  if (p.trace && blockIdx.x == 0) {
+    if (warp < C::NUM_SOFTMAX_WARPS && (threadIdx.x & 127) == 0) tr_role = warp >> 2;
+    if (warp == C::TMA_WARP && lane == 0) tr_role = 2;
+    if (warp == C::MMA_WARP && lane == 0) tr_role = 3;  // tile-0 MMA issuer
+  }
+  if (threadIdx.x < 4 && p.trace) tr_cnt[threadIdx.x] = 0;
+#endif
 
   if (threadIdx.x == 0) {
     mbar_init(&bar->q_full, 1);
-    mbar_init(&bar->q_empty, 1);
+    mbar_init(&bar->q_empty, NQ);
     mbar_init(&bar->fix, 1);
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&bar->k_full[s], 1);
       mbar_init(&bar->v_full[s], 1);
-      mbar_init(&bar->kv_empty[s], 1);
+      mbar_init(&bar->kv_empty[s], NQ);
     }
     for (int t = 0; t < 2; ++t) {
       mbar_init(&bar->s_full[t], 1);
       mbar_init(&bar->p_full[t], 4);
       mbar_init(&bar->o_full[t], 1);
       mbar_init(&bar->o_empty[t], 4);
+      mbar_init(&bar->s_free[t], 4);
+      mbar_init(&bar->pv_done[t], 1);
     }
     bar->abort_flag = 0;
     mbar_fence_init();
@@ -255,9 +297,12 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
     uint32_t fill = 0;
     for (int w = blockIdx.x; w < num_items && !failed; w += gridDim.x) {
       const Item it = decode_item<C::PAIR, BN>(p, w);
+      // All lanes wait (a converged warp polls fastest); one lane issues.
+      if (!mbar_wait(&bar->q_empty, q_empty_ph, abort_flag, tmo)) fail();
+      failed = __any_sync(0xffffffffu, failed);
+      q_empty_ph ^= 1;
       if (lane == 0) {
-        if (!mbar_wait(&bar->q_empty, q_empty_ph, abort_flag, tmo)) fail();
-        q_empty_ph ^= 1;
+        FMLM_TR(42);
         if (!failed) {
           const uint32_t nq = (it.qrows0 > 0 ? 1u : 0u) + (NQ > 1 && it.qrows1 > 0 ? 1u : 0u);
           mbar_arrive_expect_tx(&bar->q_full, nq * C::Q_BYTES);
@@ -284,8 +329,10 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
           const bool fix = sgm.fix && valid < BN;
           uint8_t* tk = sK + st * C::KV_BYTES;
           uint8_t* tv = sV + st * C::KV_BYTES;
+          if (!mbar_wait(&bar->kv_empty[st], ph ^ 1u, abort_flag, tmo)) fail();
+          failed = __any_sync(0xffffffffu, failed);
           if (lane == 0) {
-            if (!mbar_wait(&bar->kv_empty[st], ph ^ 1u, abort_flag, tmo)) fail();
+            FMLM_TR(40);
             if (!failed) {
               if (!(fix && mla)) {
                 mbar_arrive_expect_tx(&bar->k_full[st], C::KV_BYTES);
@@ -327,92 +374,145 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
         }
       }
     }
-  } else if (warp == C::MMA_WARP) {
-    // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t fmt = BF16 ? 1u : 0u;
-      constexpr uint32_t idesc_qk = make_idesc_f16(fmt, 0, 0, BM, BN);
-      constexpr uint32_t idesc_pv = make_idesc_f16(fmt, 0, 1, BM, D);
-      constexpr uint32_t layout = swizzle_code(SWB);
-      const uint32_t sQa = smem_u32(sQ), sKa = smem_u32(sK), sVa = smem_u32(sV);
-      uint32_t q_full_ph = 0, p_ph[2] = {0, 0}, o_empty_ph[2] = {1, 1};
-      uint32_t fill = 0;
+  } else if (warp >= C::MMA_WARP) {
+    // ------------------------------------------------------------ MMA issuers
+    // Warp MMA_WARP + t issues every tcgen05.mma of query tile t, so the two
+    // tiles' dependency chains (waits, issue back-pressure) run side by side.
+    // The whole warp waits (converged polling is several times cheaper than a
+    // lone lane's); one elected lane issues.
+    const int t = warp - C::MMA_WARP;
+    constexpr uint32_t fmt = BF16 ? 1u : 0u;
+    constexpr uint32_t idesc_qk = make_idesc_f16(fmt, 0, 0, BM, BN);
+    constexpr uint32_t idesc_pv = make_idesc_f16(fmt, 0, 1, BM, D);
+    constexpr uint32_t layout = swizzle_code(SWB);
+    const uint32_t sQa = smem_u32(sQ) + t * C::Q_BYTES, sKa = smem_u32(sK), sVa = smem_u32(sV);
+    const uint32_t tS_d = tmem_base + C::TM_S + t * BN;
+    const uint32_t tO_d = tmem_base + C::TM_O + t * D;
+    const uint32_t tP_a = tmem_base + (C::SEP_P ? C::TM_P + t * (BN / 2) : C::TM_S + t * BN);
+    const bool leader = elect_one();
+    uint32_t q_full_ph = 0, p_ph = 0, o_empty_ph = 1, s_free_ph = 0;
+    bool first_item = true;
+    uint32_t fill = 0;
 
-      auto issue_s = [&](int t, int st) {
-        const uint32_t d = tmem_base + C::TM_S + t * BN;
+    auto issue_s = [&](int st) {
+      if (leader) {
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t slab = (kk * 32) / SWB, inrow = (kk * 32) % SWB;
-          const uint64_t a = make_smem_desc(sQa + t * C::Q_BYTES + slab * (BM * SWB) + inrow, 16, 8 * SWB, layout);
+          const uint64_t a = make_smem_desc(sQa + slab * (BM * SWB) + inrow, 16, 8 * SWB, layout);
           const uint64_t b = make_smem_desc(sKa + st * C::KV_BYTES + slab * (BN * SWB) + inrow, 16, 8 * SWB, layout);
-          umma_ss(d, a, b, idesc_qk, kk > 0 ? 1u : 0u);
+          umma_ss(tS_d, a, b, idesc_qk, kk > 0 ? 1u : 0u);
         }
-      };
-      auto issue_pv = [&](int t, int st, bool acc) {
-        const uint32_t d = tmem_base + C::TM_O + t * D;
-        const uint32_t a_tm = tmem_base + C::TM_S + t * BN;  // P overwrites S (packed 16-bit pairs)
+      }
+    };
+    auto issue_pv = [&](int st, bool acc) {
+      if (leader) {
         const uint32_t vbase = (mla ? sKa : sVa) + st * C::KV_BYTES;
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk) {
           const uint64_t b = make_smem_desc(vbase + kk * 16 * SWB, BN * SWB, 8 * SWB, layout);
-          umma_ts(d, a_tm + kk * 8, b, idesc_pv, (acc || kk > 0) ? 1u : 0u);
+          umma_ts(tO_d, tP_a + kk * 8, b, idesc_pv, (acc || kk > 0) ? 1u : 0u);
         }
-      };
+      }
+    };
+    auto commit = [&](uint64_t* b) {
+      if (leader) umma_commit(b);
+      __syncwarp();
+    };
+    auto wait = [&](uint64_t* b, uint32_t ph) -> bool {
+      if (!mbar_wait(b, ph, abort_flag, tmo)) fail();
+      failed = __any_sync(0xffffffffu, failed);
+      return !failed;
+    };
 
-      for (int w = blockIdx.x; w < num_items && !failed; w += gridDim.x) {
-        const Item it = decode_item<C::PAIR, BN>(p, w);
-        const bool tv0 = it.qrows0 > 0, tv1 = NQ > 1 && it.qrows1 > 0;
-        const int nb = it.nblocks();
-        if (!mbar_wait(&bar->q_full, q_full_ph, abort_flag, tmo)) { fail(); break; }
-        q_full_ph ^= 1u;
-        {
-          const int st = fill % STAGES;
-          if (!mbar_wait(&bar->k_full[st], (fill / STAGES) & 1u, abort_flag, tmo)) { fail(); break; }
-          tc_fence_after();
-#pragma unroll
-          for (int t = 0; t < NQ; ++t)
-            if (t == 0 ? tv0 : tv1) { issue_s(t, st); umma_commit(&bar->s_full[t]); }
-          if (nb == 1) umma_commit(&bar->q_empty);
-        }
-        for (int j = 0; j < nb && !failed; ++j) {
+    for (int w = blockIdx.x; w < num_items && !failed; w += gridDim.x) {
+      const Item it = decode_item<C::PAIR, BN>(p, w);
+      const int nb = it.nblocks();
+      if (!wait(&bar->q_full, q_full_ph)) break;
+      q_full_ph ^= 1u;
+      if (t == 0) FMLM_TR(34);
+      if (it.qrows(t) == 0) {
+        // This tile is empty for the item: release Q and every K/V stage in
+        // order (after each fill has landed, so no release runs ahead).
+        if (leader) mbar_arrive(&bar->q_empty);
+        for (int j = 0; j < nb; ++j) {
           const int st = (fill + j) % STAGES;
-          const int st1 = (fill + j + 1) % STAGES;
-          const uint32_t ph1 = ((fill + j + 1) / STAGES) & 1u;
-          if (!mla) {
-            if (!mbar_wait(&bar->v_full[st], ((fill + j) / STAGES) & 1u, abort_flag, tmo)) { fail(); break; }
-          }
-          bool k_next_ready = false;
-#pragma unroll
-          for (int t = 0; t < NQ; ++t) {
-            if (failed || !(t == 0 ? tv0 : tv1)) continue;
-            if (!mbar_wait(&bar->p_full[t], p_ph[t], abort_flag, tmo)) { fail(); continue; }
-            p_ph[t] ^= 1u;
-            if (j == 0) {
-              if (!mbar_wait(&bar->o_empty[t], o_empty_ph[t], abort_flag, tmo)) { fail(); continue; }
-              o_empty_ph[t] ^= 1u;
-            }
-            tc_fence_after();
-            issue_pv(t, st, j > 0);
-            if (j + 1 < nb) {
-              if (!k_next_ready) {
-                if (!mbar_wait(&bar->k_full[st1], ph1, abort_flag, tmo)) { fail(); continue; }
-                tc_fence_after();
-                k_next_ready = true;
-              }
-              issue_s(t, st1);
-              umma_commit(&bar->s_full[t]);
-            } else {
-              umma_commit(&bar->o_full[t]);
-            }
-          }
-          if (failed) break;
-          if (j + 2 == nb) umma_commit(&bar->q_empty);
-          umma_commit(&bar->kv_empty[st]);
+          if (!wait(&bar->k_full[st], ((fill + j) / STAGES) & 1u)) break;
+          if (leader) mbar_arrive(&bar->kv_empty[st]);
         }
         fill += nb;
+        continue;
       }
+      {
+        const int st = fill % STAGES;
+        if (!wait(&bar->k_full[st], (fill / STAGES) & 1u)) break;
+        if (C::SEP_P && !first_item) {
+          // the softmax's read of the previous item's last S (done long ago)
+          if (!wait(&bar->s_free[t], s_free_ph)) break;
+          s_free_ph ^= 1u;
+        }
+        first_item = false;
+        tc_fence_after();
+        issue_s(st);
+        commit(&bar->s_full[t]);
+        if (nb == 1) commit(&bar->q_empty);
+      }
+      for (int j = 0; j < nb && !failed; ++j) {
+        const int st = (fill + j) % STAGES;
+        const int st1 = (fill + j + 1) % STAGES;
+        const uint32_t ph = ((fill + j) / STAGES) & 1u;
+        const uint32_t ph1 = ((fill + j + 1) / STAGES) & 1u;
+        if constexpr (C::SEP_P) {
+          // S_t(j+1) as soon as the softmax has read S_t(j) ...
+          if (j + 1 < nb) {
+            if (!wait(&bar->k_full[st1], ph1)) break;
+            if (!wait(&bar->s_free[t], s_free_ph)) break;
+            s_free_ph ^= 1u;
+            tc_fence_after();
+            issue_s(st1);
+            commit(&bar->s_full[t]);
+            if (t == 0) FMLM_TR(32);
+            if (j + 2 == nb) commit(&bar->q_empty);
+          }
+          // ... then O_t += P_t(j) V(j) once P_t(j) is in TMEM.
+          if (!mla && !wait(&bar->v_full[st], ph)) break;
+          if (!wait(&bar->p_full[t], p_ph)) break;
+          p_ph ^= 1u;
+          if (t == 0) FMLM_TR(30);
+          if (j == 0) {
+            if (!wait(&bar->o_empty[t], o_empty_ph)) break;
+            o_empty_ph ^= 1u;
+          }
+          tc_fence_after();
+          issue_pv(st, j > 0);
+          commit(&bar->pv_done[t]);
+          commit(&bar->kv_empty[st]);
+        } else {
+          if (!mla && !wait(&bar->v_full[st], ph)) break;
+          if (!wait(&bar->p_full[t], p_ph)) break;
+          p_ph ^= 1u;
+          if (t == 0) FMLM_TR(30);
+          if (j == 0) {
+            if (!wait(&bar->o_empty[t], o_empty_ph)) break;
+            o_empty_ph ^= 1u;
+          }
+          tc_fence_after();
+          issue_pv(st, j > 0);
+          if (j + 1 < nb) {
+            if (!wait(&bar->k_full[st1], ph1)) break;
+            tc_fence_after();
+            issue_s(st1);
+            commit(&bar->s_full[t]);
+            if (t == 0) FMLM_TR(32);
+          } else {
+            commit(&bar->o_full[t]);
+          }
+          if (j + 2 == nb) commit(&bar->q_empty);
+          commit(&bar->kv_empty[st]);
+        }
+      }
+      fill += nb;
     }
-    __syncwarp();
   } else {
     // ------------------------------------------------------------ softmax + epilogue
     const int t = warp >> 2;
@@ -421,10 +521,11 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
     const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
     const uint32_t tS = tmem_base + lane_off + C::TM_S + t * BN;
     const uint32_t tO = tmem_base + lane_off + C::TM_O + t * D;
+    const uint32_t tP = C::SEP_P ? tmem_base + lane_off + C::TM_P + t * (BN / 2) : tS;
     const float sl2 = p.scale_log2;
     const bool pos_scale = sl2 > 0.f;
     const float fac = pos_scale ? sl2 : 1.0f;
-    uint32_t s_ph = 0, o_ph = 0;
+    uint32_t s_ph = 0, o_ph = 0, pv_ph = 0;
     T* out = reinterpret_cast<T*>(p.out);
 
     for (int w = blockIdx.x; w < num_items && !failed; w += gridDim.x) {
@@ -443,10 +544,18 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
           if (!mbar_wait(&bar->s_full[t], s_ph, abort_flag, tmo)) { fail(); }
           failed = __any_sync(0xffffffffu, failed);
           if (failed) break;
+          FMLM_TR(10 + t);
           s_ph ^= 1u;
           tc_fence_after();
           uint32_t r[BN];
           if constexpr (BN == 128) tmem_ld_x128(tS, r); else tmem_ld_x64(tS, r);
+          FMLM_TR(12 + t);
+          if constexpr (C::SEP_P) {
+            // S_t is in registers: the MMA warp may overwrite it with S_t(j+1).
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bar->s_free[t]);
+          }
           // With a positive scale the row max is taken on raw scores and the
           // scale is folded into the exp2 argument (one FFMA per element);
           // otherwise scores are scaled first.
@@ -503,10 +612,26 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
             }
           }
           l += (sums[0] + sums[1]) + (sums[2] + sums[3]);
-          if constexpr (BN == 128) tmem_st_x64(tS, pk); else tmem_st_x32(tS, pk);
+          FMLM_TR(14 + t);
+          if constexpr (C::SEP_P) {
+            // P_t and O_t are free once PV_t(j-1) has completed.
+            if (j > 0) {
+              if (!mbar_wait(&bar->pv_done[t], pv_ph, abort_flag, tmo)) fail();
+              failed = __any_sync(0xffffffffu, failed);
+              if (failed) break;
+              pv_ph ^= 1u;
+              tc_fence_after();
+            }
+          }
+          if constexpr (BN == 128) {
+            tmem_st_x32_nowait(tP, pk);
+            tmem_st_x32_nowait(tP + 32, pk + 32);
+          } else {
+            tmem_st_x32_nowait(tP, pk);
+          }
           if (__any_sync(0xffffffffu, need)) {
-            // PV of the previous block is complete (it was issued before this
-            // block's S), and PV of this block waits for p_full: O is stable.
+            // O holds PV(0..j-1), all complete (aliased P: PV_t(j-1) was issued
+            // before S_t(j); separate P: waited above); PV_t(j) waits for p_full.
 #pragma unroll
             for (int c0 = 0; c0 < D; c0 += OC) {
               uint32_t o[OC];
@@ -516,18 +641,26 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
               tmem_st_chunk(tO + c0, o);
             }
           }
+          tmem_wait_st();
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&bar->p_full[t]);
+          FMLM_TR(16 + t);
         }
         if (failed) break;
       }
       if (failed) break;
       // epilogue: O / l  ->  global
-      if (!mbar_wait(&bar->o_full[t], o_ph, abort_flag, tmo)) fail();
+      if constexpr (C::SEP_P) {
+        if (!mbar_wait(&bar->pv_done[t], pv_ph, abort_flag, tmo)) fail();
+        pv_ph ^= 1u;
+      } else {
+        if (!mbar_wait(&bar->o_full[t], o_ph, abort_flag, tmo)) fail();
+        o_ph ^= 1u;
+      }
       failed = __any_sync(0xffffffffu, failed);
       if (failed) break;
-      o_ph ^= 1u;
+      FMLM_TR(18 + t);
       tc_fence_after();
       const float inv = (l > 0.f) ? 1.0f / l : 1.0f;
       T* orow = out + (it.out_row0 + t * BM + row) * (long long)D;
@@ -556,12 +689,25 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar->o_empty[t]);
+      FMLM_TR(20 + t);
     }
   }
 
   // ------------------------------------------------------------ teardown
+#ifdef FMLM_TRACE
+  if (tr_role >= 0) tr_cnt[tr_role] = tr_n;
+#endif
   tc_fence_before();
   __syncthreads();
+#ifdef FMLM_TRACE
+  if (p.trace && blockIdx.x == 0) {
+    for (int r = 0; r < 4; ++r) {
+      const int n = tr_cnt[r];
+      if (threadIdx.x == 0) p.trace[r] = (unsigned long long)n;
+      for (int i = threadIdx.x; i < n; i += blockDim.x) p.trace[4 + r * kTraceSlots + i] = tr_buf[r * kTraceSlots + i];
+    }
+  }
+#endif
   tc_fence_after();
   if (warp == C::MMA_WARP) {
     if (*abort_flag) {

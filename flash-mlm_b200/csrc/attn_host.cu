@@ -212,6 +212,10 @@ int kv_box_rows(int D) { return D >= 256 ? 64 : 128; }
 
 constexpr unsigned long long kTimeoutNs = 2000000000ull;  // 2 s per wait
 
+#ifdef FMLM_TRACE
+unsigned long long* g_trace_buffer = nullptr;
+#endif
+
 int check_common(int dtype, int D, const void* out) {
   if (dtype != FMLM_DTYPE_F16 && dtype != FMLM_DTYPE_BF16) return set_error(FMLM_ERR_INVALID, "dtype must be f16 or bf16");
   if (!head_dim_supported(D)) return set_error(FMLM_ERR_UNSUPPORTED, "HEAD_DIM must be one of {16, 32, 64, 128, 256}");
@@ -333,10 +337,18 @@ extern "C" int fmlm_attn_packed_fwd(const fmlm_packed_args* a, void* stream) {
   p.out = a->out;
   p.err = a->error_word;
   p.timeout_ns = kTimeoutNs;
+#ifdef FMLM_TRACE
+  p.trace = g_trace_buffer;
+#endif
   const long long items_bound = cap * (long long)a->num_heads;
   const int grid = (int)std::min<long long>(items_bound, device_sm_count());
   return a->dtype == FMLM_DTYPE_BF16 ? dispatch<true>(D, m, p, grid, s) : dispatch<false>(D, m, p, grid, s);
 }
+
+#ifdef FMLM_TRACE
+// Debug builds only: device buffer receiving the timeline of CTA 0.
+extern "C" FMLM_API void fmlm_debug_set_trace(unsigned long long* buf) { fmlm::g_trace_buffer = buf; }
+#endif
 
 extern "C" const char* fmlm_last_error(void) { return last_error_slot().c_str(); }
 
