@@ -570,12 +570,16 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
           }
           float mx;
           {
+            // 3-input max tree: BN/2 instructions in 8 independent chains.
             float m8[8];
 #pragma unroll
             for (int i = 0; i < 8; ++i) m8[i] = __uint_as_float(r[i]);
 #pragma unroll
-            for (int c = 8; c < BN; ++c) m8[c & 7] = fmaxf(m8[c & 7], __uint_as_float(r[c]));
-            mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])), fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
+            for (int c = 8; c + 1 < BN; c += 2) {
+              const int k = (c >> 1) & 7;
+              m8[k] = fmax3(m8[k], __uint_as_float(r[c]), __uint_as_float(r[c + 1]));
+            }
+            mx = fmax3(fmax3(m8[0], m8[1], m8[2]), fmax3(m8[3], m8[4], m8[5]), fmaxf(m8[6], m8[7]));
             mx *= fac;  // -inf stays -inf (fac > 0)
           }
           // Move the reference max only when this block raises it by more than 2^8.
@@ -594,21 +598,21 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
           uint32_t pk[BN / 2];
 #pragma unroll
           for (int c = 0; c < BN / 2; ++c) {
-            const float p0 = ex2_approx(fmaf(__uint_as_float(r[2 * c]), fac, neg_mu));
-            const float p1 = ex2_approx(fmaf(__uint_as_float(r[2 * c + 1]), fac, neg_mu));
-            // The row sum uses the rounded P that the MMA multiplies, so O / l
-            // is an exact convex combination of V rows with those weights.
+            const float x0 = fmaf(__uint_as_float(r[2 * c]), fac, neg_mu);
+            const float x1 = fmaf(__uint_as_float(r[2 * c + 1]), fac, neg_mu);
+            // Every fourth pair goes through the polynomial on the FMA pipe so
+            // the MUFU pipe (16 exp2 / clk / SM) is not the only limit.
+            const bool poly = (c & 3) == 3;
+            const float p0 = poly ? ex2_poly(x0) : ex2_approx(x0);
+            const float p1 = poly ? ex2_poly(x1) : ex2_approx(x1);
+            sums[(2 * c) & 3] += p0;
+            sums[(2 * c + 1) & 3] += p1;
             if constexpr (BF16) {
               __nv_bfloat162 v2 = __floats2bfloat162_rn(p0, p1);
               pk[c] = *reinterpret_cast<uint32_t*>(&v2);
-              sums[(2 * c) & 3] += __uint_as_float(pk[c] << 16);
-              sums[(2 * c + 1) & 3] += __uint_as_float(pk[c] & 0xFFFF0000u);
             } else {
               __half2 v2 = __floats2half2_rn(p0, p1);
               pk[c] = *reinterpret_cast<uint32_t*>(&v2);
-              const float2 f = __half22float2(v2);
-              sums[(2 * c) & 3] += f.x;
-              sums[(2 * c + 1) & 3] += f.y;
             }
           }
           l += (sums[0] + sums[1]) + (sums[2] + sums[3]);

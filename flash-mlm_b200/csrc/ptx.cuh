@@ -80,6 +80,16 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   }
 }
 
+// Per-warpgroup register reallocation (all four warps of a warpgroup execute it).
+template <int N>
+__device__ __forceinline__ void setmaxnreg_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <int N>
+__device__ __forceinline__ void setmaxnreg_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+
 // ---------------------------------------------------------------- fences
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -173,6 +183,27 @@ __device__ __forceinline__ uint64_t make_smem_desc(uint32_t saddr, uint32_t lbo_
 __host__ __device__ constexpr uint32_t make_idesc_f16(uint32_t ab_fmt, uint32_t a_mn, uint32_t b_mn, int M, int N) {
   return (1u << 4) | (ab_fmt << 7) | (ab_fmt << 10) | (a_mn << 15) | (b_mn << 16) |
          ((static_cast<uint32_t>(N) >> 3) << 17) | ((static_cast<uint32_t>(M) >> 4) << 24);
+}
+
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// 2^x on the FMA/ALU pipes (no MUFU): x = j + f with j = round(x) read from
+// the low mantissa bits of x + 1.5*2^23, 2^f on [-0.5, 0.5] by a degree-3
+// polynomial fitted for minimum relative error (max 7.5e-5, below the
+// f16/bf16 rounding applied to P), and j added to the exponent field.
+// Inputs below -126 are clamped (results ~1e-38 instead of 0).
+__device__ __forceinline__ float ex2_poly(float x) {
+  x = fmaxf(x, -126.0f);
+  const float t = x + 12582912.0f;
+  const float fr = x - (t - 12582912.0f);
+  float p = fmaf(0.05517132207751274f, fr, 0.24261054396629333f);
+  p = fmaf(p, fr, 0.6932609677314758f);
+  p = fmaf(p, fr, 0.9999281167984009f);
+  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
 }
 
 __device__ __forceinline__ float ex2_approx(float x) {
