@@ -350,6 +350,66 @@ extern "C" int fmlm_attn_packed_fwd(const fmlm_packed_args* a, void* stream) {
 extern "C" FMLM_API void fmlm_debug_set_trace(unsigned long long* buf) { fmlm::g_trace_buffer = buf; }
 #endif
 
+// ---------------------------------------------------------------------------
+// Allocation-free variant of fmlm_attn_packed_fwd.
+//
+// Some callers cannot call cudaMalloc at all: code running inside a CUDA
+// graph being captured, real-time or embedded hosts whose allocator is locked
+// after start-up, and plugin hosts that hand a library only pre-allocated
+// tensors.  For them the tile schedule lives in a fixed array in device
+// memory that every GPU loading this library holds until the process exits
+// (kNoAllocScheduleInts int32 = 256 KB).  The first call on a device looks the
+// array's address up with cudaGetSymbolAddress (make that first call before
+// any stream capture); later calls reuse it.  Every call shares the array and
+// the schedule kernel rewrites it completely on each call (nothing needs to
+// start at zero), so calls that overlap on the GPU (different streams,
+// different threads on one device) race and must be serialised by the caller.
+namespace fmlm {
+namespace {
+constexpr int kNoAllocScheduleInts = 65536;
+static __device__ __align__(256) int g_noalloc_schedule[kNoAllocScheduleInts];
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[64] = {};
+
+int noalloc_schedule_ptr(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return set_error(FMLM_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= 64) return set_error(FMLM_ERR_INVALID, "device index %d out of range", dev);
+  std::lock_guard<std::mutex> g(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_schedule);
+    if (e != cudaSuccess || p == nullptr)
+      return set_error(FMLM_ERR_CUDA, "cudaGetSymbolAddress(schedule scratch): %s", cudaGetErrorString(e));
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return FMLM_OK;
+}
+}  // namespace
+}  // namespace fmlm
+
+extern "C" int fmlm_attn_packed_fwd_noalloc(const fmlm_packed_args* a, void* stream) {
+  if (!a) return set_error(FMLM_ERR_INVALID, "null args");
+  const size_t have = sizeof(int) * (size_t)kNoAllocScheduleInts;
+  const size_t need = fmlm_packed_workspace_bytes(a->batch, a->total_q_len, a->head_dim);
+  if (need > have)
+    return set_error(FMLM_ERR_INVALID,
+                     "fmlm_attn_packed_fwd_noalloc: this problem needs a %zu-byte tile schedule but the built-in "
+                     "scratch holds %zu bytes (batch + total_q_len / 256 must stay below about 65500); "
+                     "use fmlm_attn_packed_fwd with a caller workspace",
+                     need, have);
+  void* ws = nullptr;
+  int rc = noalloc_schedule_ptr(&ws);
+  if (rc) return rc;
+  fmlm_packed_args b = *a;
+  b.workspace = ws;
+  b.workspace_bytes = have;
+  b.reuse_schedule = 0;
+  return fmlm_attn_packed_fwd(&b, stream);
+}
+
 extern "C" const char* fmlm_last_error(void) { return last_error_slot().c_str(); }
 
 extern "C" int fmlm_version(void) { return 100; }

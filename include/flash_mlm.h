@@ -106,6 +106,19 @@ FMLM_API int fmlm_attn_dense_fwd(const fmlm_dense_args* args, void* stream);
 /* Packed variable-length attention over [context segment ++ main segment]. */
 FMLM_API int fmlm_attn_packed_fwd(const fmlm_packed_args* args, void* stream);
 
+/* Same computation as fmlm_attn_packed_fwd, but allocation-free: `workspace`
+ * and `workspace_bytes` are ignored and the tile schedule is kept in a fixed
+ * 256 KB array in device memory that the library owns (held by every GPU that
+ * loads the library until exit).  No counterpart in the reference: it exists
+ * for callers that cannot allocate device memory (capture of a CUDA graph,
+ * hosts whose allocator is locked after start-up, plugin hosts that only pass
+ * pre-allocated buffers).  The first call on a device looks the array up
+ * (make it before any stream capture).  Problems whose schedule would exceed
+ * the array (batch + total_q_len / 256 above about 65500) are rejected with
+ * FMLM_ERR_INVALID.  All calls share the array: calls that overlap on the GPU
+ * race, so serialise them. */
+FMLM_API int fmlm_attn_packed_fwd_noalloc(const fmlm_packed_args* args, void* stream);
+
 /* Workspace size for fmlm_attn_packed_fwd (on-device tile schedule). */
 FMLM_API size_t fmlm_packed_workspace_bytes(int32_t batch, int64_t total_q_len, int32_t head_dim);
 
