@@ -77,14 +77,20 @@ struct AttnCfg {
   static constexpr int D = D_;
   static constexpr int NQ = NQ_;
   static constexpr int BM = 128;                   // query rows per tile (UMMA M)
-  static constexpr int BN = (D >= 256) ? 64 : 128; // key rows per block (UMMA N of S)
+  // D = 512 is the MLA latent width: O (128 x 512 fp32) alone would fill TMEM,
+  // so a work item accumulates one 256-column half of O (DV) and S is
+  // recomputed for the other half.  V is the K tile (MLA only).
+  static constexpr int DV = (D == 512) ? 256 : D;  // O columns per work item
+  static constexpr int NDH = D / DV;               // work items per (tile, head)
+  static constexpr bool MLA_ONLY = (D == 512);
+  static constexpr int BN = (D == 512) ? 32 : (D >= 256) ? 64 : 128;  // key rows per block (UMMA N of S)
   static constexpr int PAIR = NQ * BM;             // query rows per work item
   static constexpr int SWB = (D * 2 >= 128) ? 128 : D * 2;  // swizzle span in bytes
   static constexpr int SLAB_COLS = SWB / 2;
   static constexpr int NSLAB = D / SLAB_COLS;
   static constexpr int Q_BYTES = BM * D * 2;
   static constexpr int KV_BYTES = BN * D * 2;
-  static constexpr int STAGES = (D <= 32) ? 4 : (D <= 64) ? 3 : 2;
+  static constexpr int STAGES = (D <= 32) ? 4 : (D <= 64) ? 3 : (D == 512) ? 3 : 2;
   static constexpr int NUM_SOFTMAX_WARPS = 4 * NQ;
   static constexpr int TMA_WARP = NUM_SOFTMAX_WARPS;
   static constexpr int MMA_WARP = NUM_SOFTMAX_WARPS + 1;  // one MMA-issuing warp per tile: MMA_WARP + t
@@ -97,15 +103,15 @@ struct AttnCfg {
   // P gets its own TMEM columns when they fit (D <= 64 with two tiles, or one
   // tile): S_t(j+1) can then be issued as soon as the softmax has read S_t(j).
   // Otherwise P is written over the first BN/2 columns of S_t.
-  static constexpr bool SEP_P = NQ * (BN + D + BN / 2) <= 512;
+  static constexpr bool SEP_P = NQ * (BN + DV + BN / 2) <= 512;
   static constexpr int TM_S = 0;                   // S_t at column t*BN
-  static constexpr int TM_O = NQ * BN;             // O_t at column TM_O + t*D
-  static constexpr int TM_P = SEP_P ? NQ * (BN + D) : 0;  // P_t at TM_P + t*BN/2 (or over S_t)
-  static constexpr int TMEM_USED = NQ * (BN + D) + (SEP_P ? NQ * BN / 2 : 0);
+  static constexpr int TM_O = NQ * BN;             // O_t at column TM_O + t*DV
+  static constexpr int TM_P = SEP_P ? NQ * (BN + DV) : 0;  // P_t at TM_P + t*BN/2 (or over S_t)
+  static constexpr int TMEM_USED = NQ * (BN + DV) + (SEP_P ? NQ * BN / 2 : 0);
   static constexpr int TMEM_COLS = TMEM_USED <= 32 ? 32 : TMEM_USED <= 64 ? 64 : TMEM_USED <= 128 ? 128
                                  : TMEM_USED <= 256 ? 256 : 512;
   static_assert(TMEM_USED <= 512, "TMEM budget");
-  static constexpr int SMEM_TILES = NQ * Q_BYTES + 2 * STAGES * KV_BYTES;
+  static constexpr int SMEM_TILES = NQ * Q_BYTES + (MLA_ONLY ? 1 : 2) * STAGES * KV_BYTES;
   static constexpr int SMEM_BYTES = SMEM_TILES + 1024 /*barriers*/ + 1024 /*alignment*/;
 };
 
@@ -122,6 +128,7 @@ struct Seg {
 // role needs dynamically indexed local memory.
 struct Item {
   int qb, qh, qrow0;
+  int dh;  // which DV-wide column block of O this item produces
   int qrows0, qrows1;
   long long out_row0;
   Seg ctx, main;
@@ -136,9 +143,11 @@ struct Item {
   }
 };
 
-template <int PAIR, int BN>
+template <int PAIR, int BN, int NDH>
 __device__ __forceinline__ Item decode_item(const AttnParams& p, int w) {
   Item it;
+  it.dh = w % NDH;
+  w /= NDH;
   const int h = w % p.H;
   const int r = w / p.H;
   int b, pair, L, seq_start;
@@ -225,7 +234,7 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;
   uint8_t* sK = sQ + NQ * C::Q_BYTES;
-  uint8_t* sV = sK + STAGES * C::KV_BYTES;
+  uint8_t* sV = C::MLA_ONLY ? sK : sK + STAGES * C::KV_BYTES;
   AttnBarriers* bar = reinterpret_cast<AttnBarriers*>(sV + STAGES * C::KV_BYTES);
   volatile int* abort_flag = &bar->abort_flag;
 
@@ -281,7 +290,7 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
   tc_fence_after();
   const uint32_t tmem_base = bar->tmem_base;
 
-  const int num_items = (p.mode == 0) ? p.num_items : __ldg(p.work) * p.H;
+  const int num_items = (p.mode == 0) ? p.num_items : __ldg(p.work) * p.H * C::NDH;
   const uint64_t tmo = p.timeout_ns;
   bool failed = false;
 
@@ -296,7 +305,7 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
     uint32_t q_empty_ph = 1, fix_ph = 0;
     uint32_t fill = 0;
     for (int w = blockIdx.x; w < num_items && !failed; w += gridDim.x) {
-      const Item it = decode_item<C::PAIR, BN>(p, w);
+      const Item it = decode_item<C::PAIR, BN, C::NDH>(p, w);
       // All lanes wait (a converged warp polls fastest); one lane issues.
       if (!mbar_wait(&bar->q_empty, q_empty_ph, abort_flag, tmo)) fail();
       failed = __any_sync(0xffffffffu, failed);
@@ -383,11 +392,11 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
     const int t = warp - C::MMA_WARP;
     constexpr uint32_t fmt = BF16 ? 1u : 0u;
     constexpr uint32_t idesc_qk = make_idesc_f16(fmt, 0, 0, BM, BN);
-    constexpr uint32_t idesc_pv = make_idesc_f16(fmt, 0, 1, BM, D);
+    constexpr uint32_t idesc_pv = make_idesc_f16(fmt, 0, 1, BM, C::DV);
     constexpr uint32_t layout = swizzle_code(SWB);
     const uint32_t sQa = smem_u32(sQ) + t * C::Q_BYTES, sKa = smem_u32(sK), sVa = smem_u32(sV);
     const uint32_t tS_d = tmem_base + C::TM_S + t * BN;
-    const uint32_t tO_d = tmem_base + C::TM_O + t * D;
+    const uint32_t tO_d = tmem_base + C::TM_O + t * C::DV;
     const uint32_t tP_a = tmem_base + (C::SEP_P ? C::TM_P + t * (BN / 2) : C::TM_S + t * BN);
     const bool leader = elect_one();
     uint32_t q_full_ph = 0, p_ph = 0, o_empty_ph = 1, s_free_ph = 0;
@@ -405,9 +414,10 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
         }
       }
     };
-    auto issue_pv = [&](int st, bool acc) {
+    auto issue_pv = [&](int st, bool acc, int dh) {
       if (leader) {
-        const uint32_t vbase = (mla ? sKa : sVa) + st * C::KV_BYTES;
+        // V columns [dh*DV, dh*DV + DV) start at slab dh*DV/SLAB_COLS of the tile.
+        const uint32_t vbase = (mla ? sKa : sVa) + st * C::KV_BYTES + (dh * C::DV / C::SLAB_COLS) * (BN * SWB);
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk) {
           const uint64_t b = make_smem_desc(vbase + kk * 16 * SWB, BN * SWB, 8 * SWB, layout);
@@ -426,7 +436,7 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
     };
 
     for (int w = blockIdx.x; w < num_items && !failed; w += gridDim.x) {
-      const Item it = decode_item<C::PAIR, BN>(p, w);
+      const Item it = decode_item<C::PAIR, BN, C::NDH>(p, w);
       const int nb = it.nblocks();
       if (!wait(&bar->q_full, q_full_ph)) break;
       q_full_ph ^= 1u;
@@ -484,7 +494,7 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
             o_empty_ph ^= 1u;
           }
           tc_fence_after();
-          issue_pv(st, j > 0);
+          issue_pv(st, j > 0, it.dh);
           commit(&bar->pv_done[t]);
           commit(&bar->kv_empty[st]);
         } else {
@@ -497,7 +507,7 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
             o_empty_ph ^= 1u;
           }
           tc_fence_after();
-          issue_pv(st, j > 0);
+          issue_pv(st, j > 0, it.dh);
           if (j + 1 < nb) {
             if (!wait(&bar->k_full[st1], ph1)) break;
             tc_fence_after();
@@ -520,7 +530,7 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
     const int row = wq * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
     const uint32_t tS = tmem_base + lane_off + C::TM_S + t * BN;
-    const uint32_t tO = tmem_base + lane_off + C::TM_O + t * D;
+    const uint32_t tO = tmem_base + lane_off + C::TM_O + t * C::DV;
     const uint32_t tP = C::SEP_P ? tmem_base + lane_off + C::TM_P + t * (BN / 2) : tS;
     const float sl2 = p.scale_log2;
     const bool pos_scale = sl2 > 0.f;
@@ -529,7 +539,7 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
     T* out = reinterpret_cast<T*>(p.out);
 
     for (int w = blockIdx.x; w < num_items && !failed; w += gridDim.x) {
-      const Item it = decode_item<C::PAIR, BN>(p, w);
+      const Item it = decode_item<C::PAIR, BN, C::NDH>(p, w);
       const int nrows = it.qrows(t);
       if (nrows == 0) continue;
       const bool row_valid = row < nrows;
@@ -548,7 +558,9 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
           s_ph ^= 1u;
           tc_fence_after();
           uint32_t r[BN];
-          if constexpr (BN == 128) tmem_ld_x128(tS, r); else tmem_ld_x64(tS, r);
+          if constexpr (BN == 128) tmem_ld_x128(tS, r);
+          else if constexpr (BN == 64) tmem_ld_x64(tS, r);
+          else tmem_ld_x32(tS, r);
           FMLM_TR(12 + t);
           if constexpr (C::SEP_P) {
             // S_t is in registers: the MMA warp may overwrite it with S_t(j+1).
@@ -630,14 +642,16 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
           if constexpr (BN == 128) {
             tmem_st_x32_nowait(tP, pk);
             tmem_st_x32_nowait(tP + 32, pk + 32);
-          } else {
+          } else if constexpr (BN == 64) {
             tmem_st_x32_nowait(tP, pk);
+          } else {
+            tmem_st_x16_nowait(tP, pk);
           }
           if (__any_sync(0xffffffffu, need)) {
             // O holds PV(0..j-1), all complete (aliased P: PV_t(j-1) was issued
             // before S_t(j); separate P: waited above); PV_t(j) waits for p_full.
 #pragma unroll
-            for (int c0 = 0; c0 < D; c0 += OC) {
+            for (int c0 = 0; c0 < C::DV; c0 += OC) {
               uint32_t o[OC];
               tmem_ld_chunk(tO + c0, o);
 #pragma unroll
@@ -667,9 +681,9 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
       FMLM_TR(18 + t);
       tc_fence_after();
       const float inv = (l > 0.f) ? 1.0f / l : 1.0f;
-      T* orow = out + (it.out_row0 + t * BM + row) * (long long)D;
-#pragma unroll
-      for (int c0 = 0; c0 < D; c0 += OC) {
+      T* orow = out + (it.out_row0 + t * BM + row) * (long long)D + it.dh * C::DV;
+#pragma unroll 4
+      for (int c0 = 0; c0 < C::DV; c0 += OC) {
         uint32_t o[OC];
         tmem_ld_chunk(tO + c0, o);
         if (row_valid) {

@@ -175,7 +175,7 @@ __global__ void __launch_bounds__(kSchedThreads) sched_kernel(const int* __restr
   if (threadIdx.x == 0) work[0] = running < cap ? running : cap;
 }
 
-int head_dim_supported(int d) { return d == 16 || d == 32 || d == 64 || d == 128 || d == 256; }
+int head_dim_supported(int d) { return d == 16 || d == 32 || d == 64 || d == 128 || d == 256 || d == 512; }
 int pair_rows(int d) { return d >= 256 ? 128 : 256; }
 
 template <int D, int NQ, bool BF16>
@@ -204,11 +204,13 @@ int dispatch(int D, const CUtensorMap* m, const AttnParams& p, int grid, cudaStr
     case 64: return launch_attn<64, 2, BF16>(m, p, grid, s);
     case 128: return launch_attn<128, 2, BF16>(m, p, grid, s);
     case 256: return launch_attn<256, 1, BF16>(m, p, grid, s);
+    case 512: return launch_attn<512, 1, BF16>(m, p, grid, s);
     default: return set_error(FMLM_ERR_UNSUPPORTED, "head_dim %d is not supported", D);
   }
 }
 
-int kv_box_rows(int D) { return D >= 256 ? 64 : 128; }
+int kv_box_rows(int D) { return D == 512 ? 32 : D >= 256 ? 64 : 128; }
+int o_halves(int D) { return D == 512 ? 2 : 1; }
 
 constexpr unsigned long long kTimeoutNs = 2000000000ull;  // 2 s per wait
 
@@ -218,7 +220,8 @@ unsigned long long* g_trace_buffer = nullptr;
 
 int check_common(int dtype, int D, const void* out) {
   if (dtype != FMLM_DTYPE_F16 && dtype != FMLM_DTYPE_BF16) return set_error(FMLM_ERR_INVALID, "dtype must be f16 or bf16");
-  if (!head_dim_supported(D)) return set_error(FMLM_ERR_UNSUPPORTED, "HEAD_DIM must be one of {16, 32, 64, 128, 256}");
+  if (!head_dim_supported(D))
+    return set_error(FMLM_ERR_UNSUPPORTED, "HEAD_DIM must be one of {16, 32, 64, 128, 256} (512 with is_mla)");
   if (!out || !aligned16(out)) return set_error(FMLM_ERR_INVALID, "out must be a 16-byte aligned device pointer");
   return FMLM_OK;
 }
@@ -233,6 +236,7 @@ extern "C" int fmlm_attn_dense_fwd(const fmlm_dense_args* a, void* stream) {
   int rc = check_common(a->dtype, a->head_dim, a->out);
   if (rc) return rc;
   const int D = a->head_dim;
+  if (D == 512 && !a->is_mla) return set_error(FMLM_ERR_UNSUPPORTED, "HEAD_DIM 512 is supported for MLA only");
   if (a->batch <= 0 || a->num_heads <= 0 || a->seq_len < 0) return set_error(FMLM_ERR_INVALID, "bad B/H/N");
   if (a->seq_len == 0) return FMLM_OK;
   const bool has_ctx = !a->prefill && a->context_len > 0;
@@ -256,7 +260,7 @@ extern "C" int fmlm_attn_dense_fwd(const fmlm_dense_args* a, void* stream) {
   p.ctx_bs = a->context_batch_size;
   p.ctx_len = a->context_len;
   const int pr = pair_rows(D);
-  const long long items = (long long)a->batch * a->num_heads * ((a->seq_len + pr - 1) / pr);
+  const long long items = (long long)a->batch * a->num_heads * ((a->seq_len + pr - 1) / pr) * o_halves(D);
   if (items > 0x7fffffffLL) return set_error(FMLM_ERR_INVALID, "problem too large");
   p.num_items = (int)items;
   p.scale_log2 = a->scale * 1.4426950408889634f;
@@ -280,6 +284,7 @@ extern "C" int fmlm_attn_packed_fwd(const fmlm_packed_args* a, void* stream) {
   int rc = check_common(a->dtype, a->head_dim, a->out);
   if (rc) return rc;
   const int D = a->head_dim;
+  if (D == 512 && !a->is_mla) return set_error(FMLM_ERR_UNSUPPORTED, "HEAD_DIM 512 is supported for MLA only");
   if (a->batch <= 0 || a->num_heads <= 0) return set_error(FMLM_ERR_INVALID, "bad batch / num_heads");
   if (a->batch >= 32768) return set_error(FMLM_ERR_INVALID, "batch must be < 32768");
   if (!a->cu_seqlens_q) return set_error(FMLM_ERR_INVALID, "cu_seqlens_q is required");
@@ -340,7 +345,7 @@ extern "C" int fmlm_attn_packed_fwd(const fmlm_packed_args* a, void* stream) {
 #ifdef FMLM_TRACE
   p.trace = g_trace_buffer;
 #endif
-  const long long items_bound = cap * (long long)a->num_heads;
+  const long long items_bound = cap * (long long)a->num_heads * o_halves(D);
   const int grid = (int)std::min<long long>(items_bound, device_sm_count());
   return a->dtype == FMLM_DTYPE_BF16 ? dispatch<true>(D, m, p, grid, s) : dispatch<false>(D, m, p, grid, s);
 }

@@ -42,6 +42,15 @@ from flash_mlm.host.host_utils import (
     validate_qkv_same_shape_rank4,
 )
 
+def _validate_head_dim(d: int, is_mla: bool) -> None:
+    """The reference whitelist {16, 32, 64, 128, 256} (host_utils.py:337-339), extended
+    with 512 for MLA: the latent width of weight-absorbed MLA, which the B200
+    kernel supports by splitting O into two 256-column halves."""
+    if is_mla and d == 512:
+        return
+    validate_head_dim_supported(d)
+
+
 # Largest reference autotune BLOCK_M (mlm_kernel.py:16); decides prefill padding under auto_tune_tiles.
 _AUTO_TUNE_PAD_BLOCK_M = 128
 
@@ -100,7 +109,7 @@ def flash_attn_mlm(
     require_cuda_tensors(q, k, v, k_cache, v_cache)
     if context_batch_size is None or context_batch_size < 1:
         raise ValueError("context_batch_size must be >= 1")
-    validate_head_dim_supported(d)
+    _validate_head_dim(d, is_mla)
     q, k, v, k_cache, v_cache = make_contiguous(q, k, v, k_cache, v_cache)
     out = torch.empty_like(q)
 
@@ -237,7 +246,7 @@ def flash_attn_mlm_compressed(
         raise ValueError("num_heads must be >= 1")
     validate_packed_cache_shapes(ctx.k_cache, ctx.v_cache, num_heads=num_heads,
                                  total_context_len=int(ctx.total_context_len), head_dim=d, is_mla=is_mla)
-    validate_head_dim_supported(d)
+    _validate_head_dim(d, is_mla)
     validate_cu_seqlens_rank1_min2(cu_seqlens_q, ctx.cu_seqlens_kv)
     if ctx.context_batch_size < 1:
         raise ValueError("context_batch_size must be >= 1")
@@ -367,7 +376,7 @@ def flash_attn_mlm_precompressed(
     require_cuda_tensors(q, k, v, ctx.k_cache, ctx.v_cache, ctx.cu_seqlens_kv)
     validate_packed_cache_shapes(ctx.k_cache, ctx.v_cache, num_heads=num_heads,
                                  total_context_len=int(ctx.total_context_len), head_dim=d, is_mla=is_mla)
-    validate_head_dim_supported(d)
+    _validate_head_dim(d, is_mla)
     validate_cu_seqlens_rank1_min2(cu_seqlens_q, ctx.cu_seqlens_kv)
     if ctx.context_batch_size < 1:
         raise ValueError("context_batch_size must be >= 1")

@@ -456,3 +456,46 @@ def test_large_logits_rescale_path():
     ref = oracle.attention_dense(q.float().numpy(), k.float().numpy(), v.float().numpy(), 0.5)
     assert_close_tol(out, ref, torch.float16, "rescale")
     no_device_errors()
+
+
+# ----------------------------------------------------------------- MLA with a 512-wide latent (no reference counterpart)
+
+
+@pytest.mark.parametrize("causal", [False, True])
+def test_mla_latent512_compressed_vs_oracle(causal):
+    g = torch.Generator().manual_seed(512 + causal)
+    B, H, N, D = 3, 4, 70, 512
+    lengths = torch.tensor([70, 5, 41], dtype=torch.int32)
+    q = (_rand((B, H, N, D), torch.bfloat16, g, 0.5))
+    k = (_rand((B, 1, N, D), torch.bfloat16, g, 0.5)).expand(B, H, N, D)
+    ctx = torch.tensor([100, 0, 37], dtype=torch.int32)
+    cu_kv = torch.cat([torch.zeros(1, dtype=torch.int32), ctx.cumsum(0).to(torch.int32)])
+    tcl = int(cu_kv[-1])
+    kc = _rand((tcl, D), torch.bfloat16, g, 0.5)
+    scale = 1.0 / math.sqrt(D)
+    cache = fm().InferenceCache()
+    cache.prefill_kv_cache(0, k_cache=kc.to(DEV), total_context_len=tcl, cu_seqlens_kv=cu_kv.to(DEV),
+                           context_batch_size=B, is_mla=True, num_heads=H, head_dim=D)
+    meta = fm().build_pack_metadata(lengths.to(DEV), N, 32)
+    out = fm().flash_attn_mlm_compressed(q.to(DEV), k.to(DEV), k.to(DEV), num_heads=H, q_meta=meta, scale=scale,
+                                         inference_cache=cache, layer_id=0, is_mla=True,
+                                         causal_query_seq_attn=causal)
+    kn = k.float().numpy()
+    ref = oracle.attention_packed(q.float().numpy(), kn, kn, meta.cu_seqlens.cpu().numpy(), scale,
+                                  k_cache=kc.float().numpy(), v_cache=kc.float().numpy(), cu_kv=cu_kv.numpy(),
+                                  context_batch_size=B, total_context_len=tcl, is_mla=True,
+                                  causal_query_seq_attn=causal)
+    assert_close_tol(out, ref, torch.bfloat16, "mla512")
+    no_device_errors()
+
+
+def test_mla_latent512_dense_and_rejections():
+    g = torch.Generator().manual_seed(77)
+    B, H, N, D = 2, 3, 50, 512
+    q, k = (_rand((B, H, N, D), torch.bfloat16, g, 0.5) for _ in range(2))
+    out = fm().flash_attn_mlm(q.to(DEV), k.to(DEV), k.to(DEV), scale=0.05, is_mla=True)
+    ref = oracle.attention_dense(q.float().numpy(), k.float().numpy(), k.float().numpy(), 0.05, is_mla=True)
+    assert_close_tol(out, ref, torch.bfloat16, "mla512 dense")
+    with pytest.raises(ValueError, match="HEAD_DIM must be one of"):
+        fm().flash_attn_mlm(q.to(DEV), k.to(DEV), k.to(DEV), scale=0.05, is_mla=False)
+    no_device_errors()
