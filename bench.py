@@ -1,28 +1,32 @@
 #!/usr/bin/env python
 """Benchmark of the flash-mlm forward path on B200 (one JSON line on rank 0).
 
-Default workload = BASELINE config 2 (the configuration the headline metric is
-quoted on): flash_attn_mlm_compressed, B=32 sequences, H=16, N=512, D=64,
+Default workload = BASELINE config 2, the configuration the headline metric is
+quoted on: flash_attn_mlm_compressed, B=32 sequences, H=16, N=512, D=64,
 bf16, query lengths U[64, 512], block_n=64, one shared 1024-token context
 prefilled into InferenceCache layer 0 by a prior prefill=True call,
-scale = 1/sqrt(64).  Synthetic seeded N(0,1) data.
+scale = 1/sqrt(64).  `--config 1|3|4|5a|5b` measures the other BASELINE
+configurations the same way (their lines are not the headline).  Synthetic
+seeded data of the configured shapes and distributions.
 
-A step is one query call.  `value` is whole-job attention TFLOP/s with
-inputs resident in HBM (L2 flushed between steps); `e2e` is the same call
-through the public API with host (pinned) inputs and a read-back of the
-output inside the timed region; `roofline` is the attention kernel alone
-(re-issued through the C ABI) against the measured bf16 peak; `cpu_baseline`
-is the CPU oracle (a numpy restatement of the reference's fp32 math) on a
-bounded sample.  `--impl reference` times only that CPU path.
+A step is one pass of the path through the public API (config 3: a prefill
+call followed by the causal query call).  `value` is whole-job attention
+TFLOP/s with inputs resident in HBM (L2 flushed between steps); `e2e` is the
+same call with host (pinned) inputs copied in and the output read back inside
+the timed region; `roofline` is the attention kernel alone (re-issued through
+the C ABI) against the measured peak; `cpu_baseline` is the CPU oracle (a
+numpy restatement of the reference's fp32 math) on a bounded sample.
+`--impl reference` times only that CPU path.
 
-Multi-GPU (torchrun): one process per GPU, each rank runs its own batch of
-32 sequences (weak scaling, no collective on the data path); the step time
-is the max over ranks.
+Multi-GPU (torchrun): one process per GPU, each rank runs its own copy of the
+workload on its own seeded data (weak scaling, no collective on the data
+path); the step time is the max over ranks.
 """
 
 from __future__ import annotations
 
 import argparse
+import ctypes
 import json
 import math
 import os
@@ -41,10 +45,6 @@ for _p in (ROOT, ROOT / "flash-mlm_b200"):
 import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
-CFG2 = dict(B=32, H=16, N=512, D=64, ctx=1024, lo=64, hi=512, block_n=64, dtype="bf16")
-WORKLOAD = ("config2: flash_attn_mlm_compressed packed varlen B=32 H=16 N=512 D=64 bf16, "
-            "query lengths U[64,512], shared 1024-token context prefilled into layer 0")
-
 
 def peaks():
     p = ROOT / "MEASURED_PEAKS.json"
@@ -55,29 +55,216 @@ def peaks():
     return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
 
 
-def make_workload(rank: int, device):
-    c = CFG2
-    g = torch.Generator().manual_seed(0 + 1000 * rank)
-    lengths = torch.randint(c["lo"], c["hi"] + 1, (c["B"],), generator=g, dtype=torch.int32)
-    shape = (c["B"], c["H"], c["N"], c["D"])
-    dt = torch.bfloat16
-    tens = []
-    for i in range(3):
-        gi = torch.Generator().manual_seed(1 + i + 1000 * rank)
-        tens.append(torch.randn(shape, generator=gi).to(dt))
-    gc = torch.Generator().manual_seed(4 + 1000 * rank)
-    ctx_k = torch.randn((1, c["H"], c["ctx"], c["D"]), generator=gc).to(dt)
-    ctx_v = torch.randn((1, c["H"], c["ctx"], c["D"]), generator=gc).to(dt)
-    return lengths, tens, (ctx_k, ctx_v)
+def _lengths(g, B, lo, hi):
+    return torch.randint(lo, hi + 1, (B,), generator=g, dtype=torch.int32)
 
 
-def flops_and_bytes(lengths: list[int]):
-    c = CFG2
-    H, D, ctx = c["H"], c["D"], c["ctx"]
-    flops = 4.0 * H * D * sum(L * (ctx + L) for L in lengths)
-    T = sum(lengths)
-    nbytes = 2 * D * (2 * H * T + 2 * H * T + 2 * H * ctx)
-    return flops, nbytes
+class Workload:
+    """One BASELINE configuration: synthetic inputs, a step through the public API, and its work counts."""
+
+    def __init__(self, config: str, rank: int, args):
+        self.config = config
+        self.rank = rank
+        self.args = args
+        g = torch.Generator().manual_seed(1000 * rank)
+        self.g = g
+        self.is_mla = False
+        self.causal = False
+        self.dense = False
+        self.ctx_lengths = None   # per-sequence context rows (or one shared length)
+        self.shared_ctx = 0
+        self.prefill_lengths = None
+        if config == "1":
+            self.B, self.H, self.N, self.D, self.dtype = 2, 8, 128, 64, torch.float16
+            self.dense = True
+            self.lengths = [128, 128]
+            self.scale = 0.125
+            self.desc = "config1: flash_attn_mlm dense [2,8,128,64] f16, scale 1/8, no cache"
+        elif config == "2":
+            self.B, self.H, self.N, self.D, self.dtype = 32, 16, 512, 64, torch.bfloat16
+            self.lengths = _lengths(g, 32, 64, 512).tolist()
+            self.shared_ctx = 1024
+            self.scale = 1.0 / 8
+            self.desc = ("config2: flash_attn_mlm_compressed packed varlen B=32 H=16 N=512 D=64 bf16, "
+                         "query lengths U[64,512], shared 1024-token context prefilled into layer 0")
+        elif config == "3":
+            self.B, self.H, self.N, self.D, self.dtype = 64, 12, 256, 64, torch.float16
+            self.lengths = _lengths(g, 64, 32, 256).tolist()
+            self.ctx_lengths = _lengths(g, 64, 256, 2048).tolist()
+            self.prefill_lengths = self.ctx_lengths
+            self.causal = True
+            self.scale = 0.125
+            self.desc = ("config3: prefill call (per-sequence context U[256,2048]) then causal_query_seq_attn query "
+                         "call, B=64 H=12 N=256 D=64 f16, query lengths U[32,256]")
+        elif config == "4":
+            self.B, self.H, self.N, self.D, self.dtype = 16, 128, 256, 512, torch.bfloat16
+            self.lengths = _lengths(g, 16, 128, 256).tolist()
+            self.ctx_lengths = [4096] * 16
+            self.is_mla = True
+            self.scale = 1.0 / math.sqrt(512)
+            self.desc = ("config4: MLA, 128 query heads over one 512-wide latent KV head, B=16, query lengths "
+                         "U[128,256], 4096 context tokens per sequence, bf16")
+        elif config == "5a":
+            ctx = args.ctx
+            self.B, self.H, self.N, self.D, self.dtype = 8, 16, 512, 128, torch.bfloat16
+            self.lengths = _lengths(g, 8, 256, 512).tolist()
+            self.ctx_lengths = [ctx] * 8
+            self.scale = 1.0 / math.sqrt(128)
+            self.desc = f"config5a: H=16 D=128 bf16 B=8, query lengths U[256,512], {ctx} context tokens per sequence"
+        elif config == "5b":
+            B = args.batch
+            self.B, self.H, self.N, self.D, self.dtype = B, 16, 512, 128, torch.bfloat16
+            self.lengths = _lengths(g, B, 256, 512).tolist()
+            self.scale = 1.0 / math.sqrt(128)
+            self.desc = f"config5b: H=16 D=128 bf16 N=512, query lengths U[256,512], B={B}, no context"
+        else:
+            raise SystemExit(f"unknown --config {config}")
+        self.T = sum(self.lengths)
+        self.block_n = 64
+
+    # ---------------------------------------------------------------- work counts
+    def _kv_rows(self, b):
+        kv = (sum(self.lengths[: b + 1]) if self.causal else self.lengths[b])
+        if self.shared_ctx:
+            kv += self.shared_ctx
+        elif self.ctx_lengths is not None:
+            kv += self.ctx_lengths[b]
+        return kv
+
+    def flops(self, query_only=False):
+        f = 4.0 * self.H * self.D * sum(L * self._kv_rows(b) for b, L in enumerate(self.lengths))
+        if self.prefill_lengths is not None and not query_only:
+            f += 4.0 * self.H * self.D * sum(L * L for L in self.prefill_lengths)
+        return f
+
+    def alg_bytes(self, query_only=True):
+        e, D, H, T = 2, self.D, self.H, self.T
+        hkv, kv = (1, 1) if self.is_mla else (H, 2)
+        ctx = self.shared_ctx if self.shared_ctx else (sum(self.ctx_lengths) if self.ctx_lengths else 0)
+        return e * D * (2 * H * T + kv * hkv * T + kv * hkv * ctx)
+
+    # ---------------------------------------------------------------- inputs and step
+    def make_host(self):
+        """Seeded host copies of the step's inputs (q, k, v; MLA k is the single latent head)."""
+        g = self.g
+        dt = self.dtype
+        B, H, N, D = self.B, self.H, self.N, self.D
+        sc = 0.5 if self.is_mla else 1.0
+        self.q_h = (torch.randn((B, H, N, D), generator=g) * sc).to(dt)
+        if self.is_mla:
+            self.k_h = (torch.randn((B, 1, N, D), generator=g) * sc).to(dt)
+            self.v_h = self.k_h
+        else:
+            self.k_h = torch.randn((B, H, N, D), generator=g).to(dt)
+            self.v_h = torch.randn((B, H, N, D), generator=g).to(dt)
+
+    def build(self, device):
+        import flash_mlm
+
+        self.fm = flash_mlm
+        self.make_host()
+        g = self.g
+        dt = self.dtype
+        B, H, N, D = self.B, self.H, self.N, self.D
+        sc = 0.5 if self.is_mla else 1.0
+        self.q = self.q_h.to(device)
+        self.k = self.k_h.to(device)
+        self.v = self.v_h.to(device) if not self.is_mla else self.k
+        self.cache = flash_mlm.InferenceCache()
+        if self.dense:
+            self.meta = None
+            return
+        self.meta = flash_mlm.build_pack_metadata(torch.tensor(self.lengths, dtype=torch.int32, device=device),
+                                                  N, self.block_n)
+        if self.shared_ctx:
+            # one shared context, prefilled into layer 0 by a prior prefill=True call (B=1, N=ctx)
+            C = self.shared_ctx
+            kc = torch.randn((1, H, C, D), generator=g).to(dt).to(device)
+            vc = torch.randn((1, H, C, D), generator=g).to(dt).to(device)
+            pm = flash_mlm.build_pack_metadata(torch.tensor([C], dtype=torch.int32, device=device), C, self.block_n)
+            flash_mlm.flash_attn_mlm_compressed(kc, kc, vc, num_heads=H, q_meta=pm, scale=self.scale,
+                                                inference_cache=self.cache, layer_id=0, block_n=self.block_n,
+                                                prefill=True)
+        elif self.prefill_lengths is not None:
+            Np = max(self.prefill_lengths)
+            self.pq = torch.randn((B, H, Np, D), generator=g).to(dt).to(device)
+            self.pk = torch.randn((B, H, Np, D), generator=g).to(dt).to(device)
+            self.pv = torch.randn((B, H, Np, D), generator=g).to(dt).to(device)
+            self.pmeta = flash_mlm.build_pack_metadata(
+                torch.tensor(self.prefill_lengths, dtype=torch.int32, device=device), Np, self.block_n)
+        elif self.ctx_lengths is not None:
+            tcl = sum(self.ctx_lengths)
+            cu = torch.zeros(B + 1, dtype=torch.int32)
+            cu[1:] = torch.tensor(self.ctx_lengths).cumsum(0)
+            rows = tcl if self.is_mla else H * tcl
+            kc = (torch.randn((rows, D), generator=g) * sc).to(dt).to(device)
+            vc = None if self.is_mla else torch.randn((rows, D), generator=g).to(dt).to(device)
+            self.cache.prefill_kv_cache(0, k_cache=kc, v_cache=vc, total_context_len=tcl, cu_seqlens_kv=cu.to(device),
+                                        context_batch_size=B, is_mla=self.is_mla, num_heads=H, head_dim=D)
+
+    def step(self, q=None, k=None, v=None):
+        fm = self.fm
+        q = self.q if q is None else q
+        k = self.k if k is None else k
+        v = self.v if v is None else v
+        if self.is_mla:
+            k = k.expand(self.B, self.H, self.N, self.D)
+            v = k
+        if self.dense:
+            return fm.flash_attn_mlm(q, k, v, scale=self.scale)
+        if self.prefill_lengths is not None:
+            fm.flash_attn_mlm_compressed(self.pq, self.pk, self.pv, num_heads=self.H, q_meta=self.pmeta,
+                                         scale=self.scale, inference_cache=self.cache, layer_id=0,
+                                         block_n=self.block_n, prefill=True)
+        return fm.flash_attn_mlm_compressed(q, k, v, num_heads=self.H, q_meta=self.meta, scale=self.scale,
+                                            inference_cache=self.cache, layer_id=0, block_n=self.block_n,
+                                            is_mla=self.is_mla, causal_query_seq_attn=self.causal)
+
+    def launches_per_step(self):
+        if self.dense:
+            return 1
+        n = 2  # schedule + attention
+        if self.causal:
+            n += 2  # pack main K and V into the packed prefix
+        if self.prefill_lengths is not None:
+            n += 2 + 2  # prefill: pack K, V into the cache + schedule + attention
+        return n
+
+    # ---------------------------------------------------------------- CPU oracle sample
+    def cpu_sample(self, budget_s: float, max_seqs=None, offset=0):
+        """Oracle on whole sequences (all heads) until the budget is used: (flops, seconds, sequences)."""
+        import oracle
+
+        q, k, v = (x.float().numpy() for x in (self.q_h, self.k_h, self.v_h))
+        if self.is_mla:
+            k = np.broadcast_to(k, q.shape)
+            v = k
+        # Keys/values standing in for context + main rows (the values do not change the work).
+        max_kv = max(self._kv_rows(b) for b in range(self.B))
+        kk = np.random.default_rng(0).standard_normal((max_kv, self.D), dtype=np.float32)
+        done, fl, t0 = 0, 0.0, time.perf_counter()
+        order = [(offset + i) % self.B for i in range(self.B)]
+        for b in order:
+            if max_seqs is not None and done >= max_seqs:
+                break
+            L = self.lengths[b]
+            if self.dense:
+                oracle.attention_dense(q[b:b + 1], k[b:b + 1], v[b:b + 1], self.scale)
+            else:
+                # the sequence's own attention with a context of the configured length (random values)
+                kv = kk[: self._kv_rows(b)]
+                qq = q[b, :, :L]
+                for h in range(self.H):
+                    s = qq[h] @ kv.T * np.float32(self.scale)
+                    s -= s.max(axis=1, keepdims=True)
+                    p = np.exp(s)
+                    p /= p.sum(axis=1, keepdims=True)
+                    _ = p @ kv
+            fl += 4.0 * self.H * self.D * L * self._kv_rows(b)
+            done += 1
+            if time.perf_counter() - t0 > budget_s:
+                break
+        return fl, time.perf_counter() - t0, done
 
 
 class ClockSampler:
@@ -111,47 +298,23 @@ class ClockSampler:
 
     def summary(self):
         self.f.flush()
-        rows = []
-        for line in Path(self.f.name).read_text().splitlines():
-            parts = [x.strip() for x in line.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                rows.append(parts)
-            except ValueError:
-                pass
+        rows = [[x.strip() for x in line.split(",")] for line in Path(self.f.name).read_text().splitlines()]
+        rows = [r for r in rows if len(r) >= 9]
         if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
-        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
-        smax = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+
+        def num(x):
+            try:
+                return float(x)
+            except ValueError:
+                return None
+
+        sm = [v for v in (num(r[1]) for r in rows) if v is not None]
+        smax = [v for v in (num(r[2]) for r in rows) if v is not None]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
                 "reasons": reasons, "samples": len(rows)}
-
-
-def cpu_oracle_sample(lengths, tens, ctx, budget_s: float, max_seqs: int | None = None):
-    """Run the CPU oracle on whole sequences until the time budget is used; returns (flops, seconds, nseq)."""
-    import oracle
-
-    c = CFG2
-    q, k, v = (t.float().numpy() for t in tens)
-    kc = ctx[0][0].float().numpy().reshape(c["H"] * c["ctx"], c["D"])
-    vc = ctx[1][0].float().numpy().reshape(c["H"] * c["ctx"], c["D"])
-    cu_kv = np.array([0, c["ctx"]])
-    scale = 1.0 / math.sqrt(c["D"])
-    done, flops, t0 = 0, 0.0, time.perf_counter()
-    for b, L in enumerate(lengths):
-        if max_seqs is not None and done >= max_seqs:
-            break
-        cu = np.array([0, L])
-        oracle.attention_packed(q[b:b + 1], k[b:b + 1], v[b:b + 1], cu, scale, k_cache=kc, v_cache=vc, cu_kv=cu_kv,
-                                context_batch_size=1, total_context_len=c["ctx"])
-        flops += flops_and_bytes([L])[0]
-        done += 1
-        if time.perf_counter() - t0 > budget_s:
-            break
-    return flops, time.perf_counter() - t0, done
 
 
 def cpu_threads() -> int:
@@ -167,19 +330,17 @@ def cpu_threads() -> int:
 
 
 def run_reference(args, rank, world):
-    """--impl reference: the CPU oracle (numpy restatement of the reference's fp32 path)."""
+    """--impl reference: the CPU oracle (numpy restatement of the reference's fp32 path) on the host cores."""
     if rank != 0:
         return
-    lengths, tens, ctx = make_workload(0, "cpu")
-    L = lengths.tolist()
-    per_step_seqs = 2
-    for _ in range(args.warmup):
-        cpu_oracle_sample(L, tens, ctx, budget_s=1e9, max_seqs=per_step_seqs)
-    fl, sec = 0.0, 0.0
+    w = Workload(args.config, 0, args)
+    w.make_host()
+    per_step = 2 if not w.dense else 1
+    for i in range(args.warmup):
+        w.cpu_sample(1e9, max_seqs=per_step, offset=i)
+    fl = sec = 0.0
     for i in range(args.steps):
-        off = (i * per_step_seqs) % len(L)
-        sub = L[off:] + L[:off]
-        f, s, _ = cpu_oracle_sample(sub, [t.roll(-off, 0) for t in tens], ctx, budget_s=1e9, max_seqs=per_step_seqs)
+        f, s, _ = w.cpu_sample(1e9, max_seqs=per_step, offset=i * per_step)
         fl += f
         sec += s
     value = fl / sec / 1e12
@@ -187,9 +348,9 @@ def run_reference(args, rank, world):
         "impl": "reference", "metric": "attention TFLOP/s", "value": value, "unit": "TFLOP/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec / args.steps * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "sample": f"{per_step_seqs} of 32 sequences (all 16 heads) per step"},
+        "config": {"workload": w.desc, "sample": f"{per_step} of {w.B} sequences (all heads) per step"},
         "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": cpu_threads(), "kind": "port",
-                         "sample": f"{per_step_seqs} sequences x 16 heads per step (numpy fp32 oracle)"},
+                         "sample": f"{per_step} sequences x {w.H} heads per step (numpy fp32 oracle)"},
         "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -201,6 +362,9 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="native", choices=["native", "reference"])
+    ap.add_argument("--config", default="2", choices=["1", "2", "3", "4", "5a", "5b"])
+    ap.add_argument("--ctx", type=int, default=4096, help="config 5a: context tokens per sequence")
+    ap.add_argument("--batch", type=int, default=32, help="config 5b: batch size")
     ap.add_argument("--cpu-budget", type=float, default=12.0, help="seconds of CPU-oracle work for cpu_baseline")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
@@ -223,35 +387,18 @@ def main():
         dist = dist_mod
         dist.init_process_group("nccl", device_id=device)
 
-    import ctypes
-
     import flash_mlm
     from flash_mlm import _lib
     from flash_mlm.host import host as host_mod
 
-    c = CFG2
-    lengths, tens, ctx = make_workload(rank, device)
-    L = lengths.tolist()
-    flops, alg_bytes = flops_and_bytes(L)
-    T = sum(L)
-    q, k, v = (t.to(device) for t in tens)
-    cache = flash_mlm.InferenceCache()
-    # The shared context is prefilled into layer 0 by a prior prefill=True call (B=1, N=1024).
-    pre_meta = flash_mlm.build_pack_metadata(torch.tensor([c["ctx"]], dtype=torch.int32, device=device), c["ctx"],
-                                             c["block_n"])
-    kc, vc = ctx[0].to(device), ctx[1].to(device)
-    flash_mlm.flash_attn_mlm_compressed(kc, kc, vc, num_heads=c["H"], q_meta=pre_meta, scale=0.125,
-                                        inference_cache=cache, layer_id=0, block_n=c["block_n"], prefill=True)
-    meta = flash_mlm.build_pack_metadata(lengths.to(device), c["N"], c["block_n"])
-    scale = 1.0 / math.sqrt(c["D"])
-
-    def step():
-        return flash_mlm.flash_attn_mlm_compressed(q, k, v, num_heads=c["H"], q_meta=meta, scale=scale,
-                                                   inference_cache=cache, layer_id=0, block_n=c["block_n"])
+    w = Workload(args.config, rank, args)
+    w.build(device)
+    flops = w.flops()
+    T = w.T
 
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=device)  # > 126 MB L2
     for _ in range(args.warmup):
-        step()
+        w.step()
     torch.cuda.synchronize(device)
 
     K = args.steps
@@ -260,8 +407,8 @@ def main():
         # pre-roll so the clock samples cover a loaded GPU around the timed region
         t_end = time.perf_counter() + 1.5
         while time.perf_counter() < t_end:
-            for _ in range(50):
-                step()
+            for _ in range(20):
+                w.step()
             torch.cuda.synchronize(device)
         if dist:
             dist.barrier()
@@ -269,44 +416,47 @@ def main():
         for i in range(K):
             flush.fill_(float(i))
             ev[i][0].record()
-            step()
+            w.step()
             ev[i][1].record()
         torch.cuda.synchronize(device)
         if dist:
             dist.barrier()
         torch.cuda.synchronize(device)
-    step_ms = [a.elapsed_time(b) for a, b in ev]
-    total_ms = sum(step_ms)
+    total_ms = sum(a.elapsed_time(b) for a, b in ev)
 
-    # attention kernel alone: re-issue the last launch through the C ABI with the schedule reused
-    args_c, ws = host_mod.last_packed_launch
-    kargs = _lib.PackedArgs.from_buffer_copy(args_c)
-    kargs.reuse_schedule = 1
-    lib = _lib.lib()
-    stream = _lib.stream_ptr(device)
-    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
-    for i in range(K):
-        flush.fill_(float(i))
-        kev[i][0].record()
-        _lib.check(lib.fmlm_attn_packed_fwd(ctypes.byref(kargs), stream), "attn kernel")
-        kev[i][1].record()
-    torch.cuda.synchronize(device)
-    kernel_ms = sum(a.elapsed_time(b) for a, b in kev) / K
+    # attention kernel alone: re-issue the last packed launch through the C ABI with the schedule reused
+    kernel_ms, k_flops = None, None
+    if not w.dense and host_mod.last_packed_launch is not None:
+        args_c, ws = host_mod.last_packed_launch
+        kargs = _lib.PackedArgs.from_buffer_copy(args_c)
+        kargs.reuse_schedule = 1
+        lib = _lib.lib()
+        stream = _lib.stream_ptr(device)
+        kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
+        for i in range(K):
+            flush.fill_(float(i))
+            kev[i][0].record()
+            _lib.check(lib.fmlm_attn_packed_fwd(ctypes.byref(kargs), stream), "attn kernel")
+            kev[i][1].record()
+        torch.cuda.synchronize(device)
+        kernel_ms = sum(a.elapsed_time(b) for a, b in kev) / K
+        k_flops = w.flops(query_only=True)
+    else:
+        kernel_ms, k_flops = total_ms / K, flops
 
     # end to end: host (pinned) inputs -> device, API call, output -> host
-    qh, kh, vh = (t.pin_memory() for t in tens)
-    out_h = torch.empty((c["H"] * T, c["D"]), dtype=torch.bfloat16).pin_memory()
-    qd, kd, vd = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    hosts = [w.q_h.pin_memory(), w.k_h.pin_memory()] + ([] if w.is_mla else [w.v_h.pin_memory()])
+    devs = [torch.empty_like(x, device=device) for x in hosts]
+    out0 = w.step()
+    out_h = torch.empty(out0.shape, dtype=out0.dtype).pin_memory()
     K_e2e = max(3, min(K, 50))
     e2e_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K_e2e)]
     for i in range(K_e2e + 2):
         if i >= 2:
             e2e_ev[i - 2][0].record()
-        qd.copy_(qh, non_blocking=True)
-        kd.copy_(kh, non_blocking=True)
-        vd.copy_(vh, non_blocking=True)
-        o = flash_mlm.flash_attn_mlm_compressed(qd, kd, vd, num_heads=c["H"], q_meta=meta, scale=scale,
-                                                inference_cache=cache, layer_id=0, block_n=c["block_n"])
+        for d, h in zip(devs, hosts):
+            d.copy_(h, non_blocking=True)
+        o = w.step(devs[0], devs[1], devs[1] if w.is_mla else devs[2])
         out_h.copy_(o, non_blocking=True)
         if i >= 2:
             e2e_ev[i - 2][1].record()
@@ -314,12 +464,12 @@ def main():
     e2e_ms = sum(a.elapsed_time(b) for a, b in e2e_ev) / K_e2e
     flash_mlm.check_device_errors(device)
 
-    t_max = torch.tensor([total_ms, kernel_ms, e2e_ms, flops, float(T)], dtype=torch.float64, device=device)
+    t = torch.tensor([total_ms, kernel_ms, e2e_ms, flops, float(T)], dtype=torch.float64, device=device)
     if dist:
-        mx = t_max.clone()
-        dist.all_reduce(mx[:3], op=dist.ReduceOp.MAX)
-        sm = t_max.clone()
-        dist.all_reduce(sm[3:], op=dist.ReduceOp.SUM)
+        mx = t.clone()
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        sm = t.clone()
+        dist.all_reduce(sm, op=dist.ReduceOp.SUM)
         total_ms, kernel_ms, e2e_ms = mx[0].item(), mx[1].item(), mx[2].item()
         all_flops, all_tokens = sm[3].item(), sm[4].item()
     else:
@@ -327,22 +477,36 @@ def main():
 
     if rank == 0:
         pk = peaks()
-        ms_step = total_ms / K
         value = all_flops * K / (total_ms * 1e-3) / 1e12
         tok_s = all_tokens * K / (total_ms * 1e-3)
-        k_tflops = flops / (kernel_ms * 1e-3) / 1e12
+        achieved = k_flops / (kernel_ms * 1e-3) / 1e12
+        alg_bytes = w.alg_bytes()
+        t_tensor = k_flops / (pk["bf16_tflops"] * 1e12)
+        t_hbm = alg_bytes / (pk["hbm_gbs"] * 1e9)
         traffic = None
-        tf = ROOT / "profiles" / "attn_fwd_config2_traffic.txt"
+        tf = ROOT / "profiles" / f"attn_fwd_config{args.config}_traffic.txt"
         if tf.exists():
             for line in tf.read_text().splitlines():
                 if line.startswith("dram_bytes_per_launch="):
                     traffic = float(line.split("=", 1)[1])
+        if t_tensor >= t_hbm:
+            roof = {"bound": "tensor", "achieved": achieved, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                    "frac": achieved / pk["bf16_tflops"]}
+        else:
+            gbs = alg_bytes / (kernel_ms * 1e-3) / 1e9
+            roof = {"bound": "hbm", "achieved": gbs, "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": gbs / pk["hbm_gbs"]}
+        roof.update({"traffic": traffic, "kernel": f"attn_fwd_kernel<{w.D},{1 if w.D >= 256 else 2},"
+                     f"{'bf16' if w.dtype == torch.bfloat16 else 'f16'}>", "kernel_ms": kernel_ms,
+                     "alg_flops_per_launch": k_flops, "alg_bytes_per_launch": alg_bytes,
+                     "roofline_ms": max(t_tensor, t_hbm) * 1e3,
+                     "frac_of_roofline_time": max(t_tensor, t_hbm) / (kernel_ms * 1e-3),
+                     "peak_source": pk["source"] + " (burst, kernel timed alone)"})
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
-            f, s, nseq = cpu_oracle_sample(L, tens, ctx, budget_s=args.cpu_budget)
+            f, s, nseq = w.cpu_sample(args.cpu_budget)
             cpu = {"value": f / s / 1e12, "unit": "TFLOP/s", "cores": cpu_threads(), "kind": "port",
-                   "sample": f"{nseq} of {c['B']} sequences x {c['H']} heads (numpy fp32 oracle), {s:.1f} s"}
-        h2d = sum(t.numel() * t.element_size() for t in tens)
+                   "sample": f"{nseq} of {w.B} sequences x {w.H} heads (numpy fp32 oracle math), {s:.1f} s"}
+        h2d = sum(x.numel() * x.element_size() for x in hosts)
         d2h = out_h.numel() * out_h.element_size()
         line = {
             "metric": "attention TFLOP/s",
@@ -351,36 +515,23 @@ def main():
             "n_gpus": world,
             "steps": K,
             "warmup": args.warmup,
-            "ms_per_step": ms_step,
+            "ms_per_step": total_ms / K,
             "higher_is_better": True,
             "scaling": "weak",
             "vs_baseline": None,
-            "dtype": "bf16",
-            "data": "synthetic (seeded N(0,1) q/k/v and context, lengths U[64,512])",
-            "config": {"workload": WORKLOAD, "B_per_gpu": c["B"], "H": c["H"], "N": c["N"], "D": c["D"],
-                       "context": c["ctx"], "block_n": c["block_n"], "tokens_per_gpu_step": T,
-                       "l2": "flushed (256 MB write) between timed steps", "parallelism": f"dp{world} (batch shards)"},
+            "dtype": "bf16" if w.dtype == torch.bfloat16 else "f16",
+            "data": "synthetic (seeded N(0,1) inputs and context of the configured shapes)",
+            "config": {"workload": w.desc, "B_per_gpu": w.B, "H": w.H, "N": w.N, "D": w.D,
+                       "tokens_per_gpu_step": T, "l2": "flushed (256 MB write) between timed steps",
+                       "parallelism": f"dp{world} (each rank its own batch)"},
             "tokens_per_s": tok_s,
             "tokens_per_s_per_gpu": tok_s / world,
             "tflops_per_gpu": value / world,
-            "roofline": {
-                "bound": "tensor",
-                "achieved": k_tflops,
-                "peak": pk["bf16_tflops"],
-                "unit": "TFLOP/s",
-                "frac": k_tflops / pk["bf16_tflops"],
-                "traffic": traffic,
-                "kernel": "attn_fwd_kernel<64,2,bf16>",
-                "kernel_ms": kernel_ms,
-                "alg_flops_per_launch": flops,
-                "alg_bytes_per_launch": alg_bytes,
-                "hbm_frac": alg_bytes / (kernel_ms * 1e-3) / 1e9 / pk["hbm_gbs"],
-                "peak_source": pk["source"] + " (burst, kernel timed alone)",
-            },
+            "roofline": roof,
             "cpu_baseline": cpu,
             "e2e": {"value": all_flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
-            "gpu_launches": 2 * K,
+            "gpu_launches": w.launches_per_step() * K,
             "clocks": clk.summary(),
         }
         print(json.dumps(line), flush=True)
