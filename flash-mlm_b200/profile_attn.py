@@ -6,7 +6,8 @@ capture the attention kernel on exactly that input.
     python flash-mlm_b200/profile_attn.py --config 2 --warmup 2 --iters 1
 
 Configs: 1 dense [2,8,128,64] f16; 2 packed B=32 H=16 N=512
-D=64 bf16 + shared 1024 context; 3 packed causal B=64 H=12 N=256 D=64 f16 +
+D=64 bf16 + shared 1024 context; 4 MLA B=16 H=128 D=512 + 4096 context per
+sequence; 3 packed causal B=64 H=12 N=256 D=64 f16 +
 per-sequence context U[256,2048]; 5a packed B=8 H=16 N=512 D=128 bf16 +
 per-sequence context --ctx; 5b packed B=--batch H=16 N=512 D=128 bf16, no context.
 Equivalent of the reference's src/profile/profile_mlm_ncu.py.
@@ -36,6 +37,21 @@ def build(config: str, ctx: int, batch: int, device):
     if config == "1":
         q, k, v = (torch.randn((2, 8, 128, 64), generator=g).to(torch.float16).to(device) for _ in range(3))
         return lambda: flash_mlm.flash_attn_mlm(q, k, v, scale=0.125)
+    if config == "4":
+        B, H, N, D = 16, 128, 256, 512
+        lengths = _lengths(g, B, 128, 256)
+        q = (torch.randn((B, H, N, D), generator=g) * 0.5).to(torch.bfloat16).to(device)
+        k = (torch.randn((B, 1, N, D), generator=g) * 0.5).to(torch.bfloat16).to(device).expand(B, H, N, D)
+        ctx = 4096
+        cu_kv = torch.arange(B + 1, dtype=torch.int32) * ctx
+        kc = (torch.randn((B * ctx, D), generator=g) * 0.5).to(torch.bfloat16).to(device)
+        cache = flash_mlm.InferenceCache()
+        cache.prefill_kv_cache(0, k_cache=kc, total_context_len=B * ctx, cu_seqlens_kv=cu_kv.to(device),
+                               context_batch_size=B, is_mla=True, num_heads=H, head_dim=D)
+        meta = flash_mlm.build_pack_metadata(lengths.to(device), N, 64)
+        return lambda: flash_mlm.flash_attn_mlm_compressed(q, k, k, num_heads=H, q_meta=meta, scale=D ** -0.5,
+                                                           inference_cache=cache, layer_id=0, block_n=64,
+                                                           is_mla=True)
     if config == "2":
         B, H, N, D, C, lo, hi, dt = 32, 16, 512, 64, 1024, 64, 512, torch.bfloat16
     elif config == "3":
