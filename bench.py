@@ -382,6 +382,7 @@ def main():
     device = torch.device("cuda", local_rank)
     dist = None
     if world > 1:
+        os.environ.setdefault("NCCL_DEBUG", "WARN")  # keep NCCL's version banner off stdout (one JSON line)
         import torch.distributed as dist_mod
 
         dist = dist_mod
