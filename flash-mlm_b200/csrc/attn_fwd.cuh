@@ -83,21 +83,28 @@ struct AttnCfg {
   static constexpr int DV = (D == 512) ? 256 : D;  // O columns per work item
   static constexpr int NDH = D / DV;               // work items per (tile, head)
   static constexpr bool MLA_ONLY = (D == 512);
-  static constexpr int BN = (D == 512) ? 32 : (D >= 256) ? 64 : 128;  // key rows per block (UMMA N of S)
+#ifndef FMLM_BN_D128
+#define FMLM_BN_D128 128
+#endif
+  static constexpr int BN = (D == 512) ? 32 : (D >= 256) ? 64 : (D == 128) ? FMLM_BN_D128 : 128;  // key rows per block
   static constexpr int PAIR = NQ * BM;             // query rows per work item
   static constexpr int SWB = (D * 2 >= 128) ? 128 : D * 2;  // swizzle span in bytes
   static constexpr int SLAB_COLS = SWB / 2;
   static constexpr int NSLAB = D / SLAB_COLS;
   static constexpr int Q_BYTES = BM * D * 2;
   static constexpr int KV_BYTES = BN * D * 2;
-  static constexpr int STAGES = (D <= 32) ? 4 : (D <= 64) ? 3 : (D == 512) ? 3 : 2;
+  // One tile per CTA at D <= 64 runs two CTAs per SM (TMEM 256 columns and
+  // about 80 KB of shared memory each): the two CTAs work on independent items.
+  static constexpr int CTAS_PER_SM = (NQ == 1 && D <= 64) ? 2 : 1;
+  static constexpr int STAGES = (CTAS_PER_SM == 2) ? 2 : (D <= 32) ? 4 : (D <= 64) ? 3 : (D == 512) ? 3
+                              : (D == 128 && BN == 64) ? 4 : 2;
   static constexpr int NUM_SOFTMAX_WARPS = 4 * NQ;
   static constexpr int TMA_WARP = NUM_SOFTMAX_WARPS;
   static constexpr int MMA_WARP = NUM_SOFTMAX_WARPS + 1;  // one MMA-issuing warp per tile: MMA_WARP + t
   static constexpr int THREADS = 32 * (NUM_SOFTMAX_WARPS + 1 + NQ);
   // Each SM sub-partition owns a quarter of the register file and every
   // fourth warp of the CTA, so the budget is 16384 / (32 * ceil(warps / 4)).
-  static constexpr int WARPS_PER_SMSP = (NUM_SOFTMAX_WARPS + 1 + NQ + 3) / 4;
+  static constexpr int WARPS_PER_SMSP = (CTAS_PER_SM * (NUM_SOFTMAX_WARPS + 1 + NQ) + 3) / 4;
   static constexpr int MAX_REGS = (16384 / (32 * WARPS_PER_SMSP)) / 8 * 8 > 255 ? 255
                                 : (16384 / (32 * WARPS_PER_SMSP)) / 8 * 8;
   // P gets its own TMEM columns when they fit (D <= 64 with two tiles, or one
@@ -606,41 +613,10 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
             m = mx;
           }
           const float neg_mu = (m == -INFINITY) ? 0.f : -m;
-          float sums[4] = {0.f, 0.f, 0.f, 0.f};
-          uint32_t pk[BN / 2];
-#pragma unroll
-          for (int c = 0; c < BN / 2; ++c) {
-            const float x0 = fmaf(__uint_as_float(r[2 * c]), fac, neg_mu);
-            const float x1 = fmaf(__uint_as_float(r[2 * c + 1]), fac, neg_mu);
-            // A share of the pairs (FMLM_POLY_MODE: 0 none, 1 one in four,
-            // 2 three in eight, 3 one in two) goes through the polynomial on
-            // the FMA pipe so the MUFU pipe (16 exp2 / clk / SM) is not the
-            // only limit.
-#ifndef FMLM_POLY_MODE
-#define FMLM_POLY_MODE 1  // measured: helps a little at D=64, hurts at D=128 (applied for D <= 64 only)
-#endif
-            const int k8 = c & 7;
-            const bool poly = D > 64                ? false
-                              : FMLM_POLY_MODE == 1 ? (c & 3) == 3
-                              : FMLM_POLY_MODE == 2 ? (k8 == 1 || k8 == 4 || k8 == 6)
-                              : FMLM_POLY_MODE == 3 ? (c & 1) == 1
-                                                    : false;
-            const float p0 = poly ? ex2_poly(x0) : ex2_approx(x0);
-            const float p1 = poly ? ex2_poly(x1) : ex2_approx(x1);
-            sums[(2 * c) & 3] += p0;
-            sums[(2 * c + 1) & 3] += p1;
-            if constexpr (BF16) {
-              __nv_bfloat162 v2 = __floats2bfloat162_rn(p0, p1);
-              pk[c] = *reinterpret_cast<uint32_t*>(&v2);
-            } else {
-              __half2 v2 = __floats2half2_rn(p0, p1);
-              pk[c] = *reinterpret_cast<uint32_t*>(&v2);
-            }
-          }
-          l += (sums[0] + sums[1]) + (sums[2] + sums[3]);
-          FMLM_TR(14 + t);
           if constexpr (C::SEP_P) {
-            // P_t and O_t are free once PV_t(j-1) has completed.
+            // P_t and O_t are free once PV_t(j-1) has completed (almost always
+            // by now); waiting first lets each half of P be stored as soon as
+            // it is packed.
             if (j > 0) {
               if (!mbar_wait(&bar->pv_done[t], pv_ph, abort_flag, tmo)) fail();
               failed = __any_sync(0xffffffffu, failed);
@@ -649,14 +625,48 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
               tc_fence_after();
             }
           }
-          if constexpr (BN == 128) {
-            tmem_st_x32_nowait(tP, pk);
-            tmem_st_x32_nowait(tP + 32, pk + 32);
-          } else if constexpr (BN == 64) {
-            tmem_st_x32_nowait(tP, pk);
-          } else {
-            tmem_st_x16_nowait(tP, pk);
+#ifndef FMLM_POLY_MODE
+#define FMLM_POLY_MODE 1  // measured: helps a little at D=64, hurts at D=128 (applied for D <= 64 only)
+#endif
+          float sums[4] = {0.f, 0.f, 0.f, 0.f};
+          // P in chunks of up to 32 packed columns (64 scores), each stored to
+          // TMEM as soon as it is ready, so at most one chunk of packed P is live.
+          constexpr int PC = BN / 2 < 32 ? BN / 2 : 32;
+#pragma unroll
+          for (int h0 = 0; h0 < BN / 2; h0 += PC) {
+            uint32_t pk[PC];
+#pragma unroll
+            for (int cc = 0; cc < PC; ++cc) {
+              const int c = h0 + cc;
+              const float x0 = fmaf(__uint_as_float(r[2 * c]), fac, neg_mu);
+              const float x1 = fmaf(__uint_as_float(r[2 * c + 1]), fac, neg_mu);
+              // A share of the pairs (FMLM_POLY_MODE: 0 none, 1 one in four,
+              // 2 three in eight, 3 one in two) goes through the polynomial on
+              // the FMA pipe so the MUFU pipe (16 exp2 / clk / SM) is not the
+              // only limit.
+              const int k8 = c & 7;
+              const bool poly = D > 64                ? false
+                                : FMLM_POLY_MODE == 1 ? (c & 3) == 3
+                                : FMLM_POLY_MODE == 2 ? (k8 == 1 || k8 == 4 || k8 == 6)
+                                : FMLM_POLY_MODE == 3 ? (c & 1) == 1
+                                                      : false;
+              const float p0 = poly ? ex2_poly(x0) : ex2_approx(x0);
+              const float p1 = poly ? ex2_poly(x1) : ex2_approx(x1);
+              sums[(2 * c) & 3] += p0;
+              sums[(2 * c + 1) & 3] += p1;
+              if constexpr (BF16) {
+                __nv_bfloat162 v2 = __floats2bfloat162_rn(p0, p1);
+                pk[cc] = *reinterpret_cast<uint32_t*>(&v2);
+              } else {
+                __half2 v2 = __floats2half2_rn(p0, p1);
+                pk[cc] = *reinterpret_cast<uint32_t*>(&v2);
+              }
+            }
+            if constexpr (PC == 32) tmem_st_x32_nowait(tP + h0, pk);
+            else tmem_st_x16_nowait(tP + h0, pk);
           }
+          l += (sums[0] + sums[1]) + (sums[2] + sums[3]);
+          FMLM_TR(14 + t);
           if (__any_sync(0xffffffffu, need)) {
             // O holds PV(0..j-1), all complete (aliased P: PV_t(j-1) was issued
             // before S_t(j); separate P: waited above); PV_t(j) waits for p_full.

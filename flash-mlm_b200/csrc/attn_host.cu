@@ -176,14 +176,21 @@ __global__ void __launch_bounds__(kSchedThreads) sched_kernel(const int* __restr
 }
 
 int head_dim_supported(int d) { return d == 16 || d == 32 || d == 64 || d == 128 || d == 256 || d == 512; }
-int pair_rows(int d) { return d >= 256 ? 128 : 256; }
+#ifndef FMLM_NQ_D64
+#define FMLM_NQ_D64 1  // one tile per CTA, two CTAs per SM (measured faster than two tiles per CTA)
+#endif
+// Query tiles (of 128 rows) per work item for a head dimension.
+int nq_for(int d) { return d >= 256 ? 1 : d == 64 ? FMLM_NQ_D64 : 2; }
+int pair_rows(int d) { return 128 * nq_for(d); }
 
 template <int D, int NQ, bool BF16>
-int launch_attn(const CUtensorMap* m, const AttnParams& p, int grid, cudaStream_t s) {
+int launch_attn(const CUtensorMap* m, const AttnParams& p, long long items, cudaStream_t s) {
   using C = AttnCfg<D, NQ>;
   auto kern = attn_fwd_kernel<D, NQ, BF16>;
-  // At least 116 KB so that exactly one CTA (and one TMEM owner) lives per SM.
-  const int smem = std::max(C::SMEM_BYTES, 116 * 1024);
+  // Shared memory is padded so that exactly CTAS_PER_SM CTAs (TMEM owners)
+  // fit on an SM: more would block in tcgen05.alloc.
+  const int smem = C::CTAS_PER_SM == 1 ? std::max(C::SMEM_BYTES, 116 * 1024) : std::max(C::SMEM_BYTES, 80 * 1024);
+  const int grid = (int)std::min<long long>(items, (long long)device_sm_count() * C::CTAS_PER_SM);
   static bool configured[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -197,19 +204,22 @@ int launch_attn(const CUtensorMap* m, const AttnParams& p, int grid, cudaStream_
 }
 
 template <bool BF16>
-int dispatch(int D, const CUtensorMap* m, const AttnParams& p, int grid, cudaStream_t s) {
+int dispatch(int D, const CUtensorMap* m, const AttnParams& p, long long items, cudaStream_t s) {
   switch (D) {
-    case 16: return launch_attn<16, 2, BF16>(m, p, grid, s);
-    case 32: return launch_attn<32, 2, BF16>(m, p, grid, s);
-    case 64: return launch_attn<64, 2, BF16>(m, p, grid, s);
-    case 128: return launch_attn<128, 2, BF16>(m, p, grid, s);
-    case 256: return launch_attn<256, 1, BF16>(m, p, grid, s);
-    case 512: return launch_attn<512, 1, BF16>(m, p, grid, s);
+    case 16: return launch_attn<16, 2, BF16>(m, p, items, s);
+    case 32: return launch_attn<32, 2, BF16>(m, p, items, s);
+    case 64: return launch_attn<64, FMLM_NQ_D64, BF16>(m, p, items, s);
+    case 128: return launch_attn<128, 2, BF16>(m, p, items, s);
+    case 256: return launch_attn<256, 1, BF16>(m, p, items, s);
+    case 512: return launch_attn<512, 1, BF16>(m, p, items, s);
     default: return set_error(FMLM_ERR_UNSUPPORTED, "head_dim %d is not supported", D);
   }
 }
 
-int kv_box_rows(int D) { return D == 512 ? 32 : D >= 256 ? 64 : 128; }
+#ifndef FMLM_BN_D128
+#define FMLM_BN_D128 128
+#endif
+int kv_box_rows(int D) { return D == 512 ? 32 : D >= 256 ? 64 : D == 128 ? FMLM_BN_D128 : 128; }
 int o_halves(int D) { return D == 512 ? 2 : 1; }
 
 constexpr unsigned long long kTimeoutNs = 2000000000ull;  // 2 s per wait
@@ -268,13 +278,12 @@ extern "C" int fmlm_attn_dense_fwd(const fmlm_dense_args* a, void* stream) {
   if (!a->error_word) return set_error(FMLM_ERR_INVALID, "error_word is required");
   p.err = a->error_word;
   p.timeout_ns = kTimeoutNs;
-  const int grid = (int)std::min<long long>(items, device_sm_count());
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  return a->dtype == FMLM_DTYPE_BF16 ? dispatch<true>(D, m, p, grid, s) : dispatch<false>(D, m, p, grid, s);
+  return a->dtype == FMLM_DTYPE_BF16 ? dispatch<true>(D, m, p, items, s) : dispatch<false>(D, m, p, items, s);
 }
 
 extern "C" size_t fmlm_packed_workspace_bytes(int32_t batch, int64_t total_q_len, int32_t head_dim) {
-  const int64_t pr = head_dim >= 256 ? 128 : 256;
+  const int64_t pr = head_dim > 0 ? pair_rows(head_dim) : 128;
   const int64_t cap = total_q_len / pr + batch + 2;
   return (size_t)((cap + 2) * sizeof(int32_t) + 15) / 16 * 16;
 }
@@ -346,8 +355,8 @@ extern "C" int fmlm_attn_packed_fwd(const fmlm_packed_args* a, void* stream) {
   p.trace = g_trace_buffer;
 #endif
   const long long items_bound = cap * (long long)a->num_heads * o_halves(D);
-  const int grid = (int)std::min<long long>(items_bound, device_sm_count());
-  return a->dtype == FMLM_DTYPE_BF16 ? dispatch<true>(D, m, p, grid, s) : dispatch<false>(D, m, p, grid, s);
+  return a->dtype == FMLM_DTYPE_BF16 ? dispatch<true>(D, m, p, items_bound, s)
+                                     : dispatch<false>(D, m, p, items_bound, s);
 }
 
 #ifdef FMLM_TRACE
@@ -402,7 +411,7 @@ extern "C" int fmlm_attn_packed_fwd_noalloc(const fmlm_packed_args* a, void* str
   if (need > have)
     return set_error(FMLM_ERR_INVALID,
                      "fmlm_attn_packed_fwd_noalloc: this problem needs a %zu-byte tile schedule but the built-in "
-                     "scratch holds %zu bytes (batch + total_q_len / 256 must stay below about 65500); "
+                     "scratch holds %zu bytes (batch + total_q_len / 128 must stay below about 65500); "
                      "use fmlm_attn_packed_fwd with a caller workspace",
                      need, have);
   void* ws = nullptr;

@@ -114,7 +114,7 @@ FMLM_API int fmlm_attn_packed_fwd(const fmlm_packed_args* args, void* stream);
  * hosts whose allocator is locked after start-up, plugin hosts that only pass
  * pre-allocated buffers).  The first call on a device looks the array up
  * (make it before any stream capture).  Problems whose schedule would exceed
- * the array (batch + total_q_len / 256 above about 65500) are rejected with
+ * the array (batch + total_q_len / 128 above about 65500) are rejected with
  * FMLM_ERR_INVALID.  All calls share the array: calls that overlap on the GPU
  * race, so serialise them. */
 FMLM_API int fmlm_attn_packed_fwd_noalloc(const fmlm_packed_args* args, void* stream);
