@@ -31,7 +31,13 @@
 namespace fmlm {
 
 // Error codes written to the device error word.
-enum : int { kErrTimeout = 1 };
+enum : int { kErrTimeout = 1, kErrSmemAlign = 2 };
+
+// Packed-mode workspace (int32): [0] entry count, [1] next-item counter,
+// [2] CTAs finished, [3] unused, then one (b << 16 | pair) entry per query
+// pair.  The schedule kernel zeroes [1] and [2]; the last CTA of each
+// attention launch zeroes them again, so a reused schedule starts clean.
+constexpr int kWorkHeader = 4;
 
 struct AttnParams {
   int mode;         // 0 = dense [B,H,N,D] rows; 1 = packed variable-length (cu_seqlens_q)
@@ -48,7 +54,7 @@ struct AttnParams {
   float scale_log2; // scale * log2(e)
   const int* cu_q;  // [B+1] packed query offsets
   const int* cu_kv; // context offsets (packed)
-  const int* work;  // packed: [0] = entry count, [1..] = (b << 16 | pair) entries
+  int* work;        // packed: schedule workspace (layout at kWorkHeader)
   void* out;        // [rows, D]
   int* err;         // device error word
   unsigned long long timeout_ns;
@@ -60,7 +66,12 @@ struct AttnParams {
 // to its own shared-memory slice; the slices are copied to p.trace at exit
 // (p.trace[0..3] = record counts, role r's records from 4 + r * kTraceSlots).
 #ifdef FMLM_TRACE
-constexpr int kTraceSlots = 1024;
+#ifndef FMLM_TRACE_SLOTS
+#define FMLM_TRACE_SLOTS 1024
+#endif
+// FMLM_TRACE_SLOTS = 0 records only per-CTA entry/exit times (no static
+// shared memory, so the occupancy is that of the product build).
+constexpr int kTraceSlots = FMLM_TRACE_SLOTS;
 #define FMLM_TR(ev)                                                                                   \
   do {                                                                                                \
     if (tr_role >= 0 && tr_n < kTraceSlots)                                                           \
@@ -96,14 +107,20 @@ struct AttnCfg {
   // One tile per CTA at D <= 64 runs two CTAs per SM (TMEM 256 columns and
   // about 80 KB of shared memory each): the two CTAs work on independent items.
   static constexpr int CTAS_PER_SM = (NQ == 1 && D <= 64) ? 2 : 1;
-  static constexpr int STAGES = (CTAS_PER_SM == 2) ? 2 : (D <= 32) ? 4 : (D <= 64) ? 3 : (D == 512) ? 3
+#ifndef FMLM_STAGES_2CTA
+#define FMLM_STAGES_2CTA 3
+#endif
+  static constexpr int STAGES = (CTAS_PER_SM == 2) ? FMLM_STAGES_2CTA : (D <= 32) ? 4 : (D <= 64) ? 3 : (D == 512) ? 3
                               : (D == 128 && BN == 64) ? 4 : 2;
   static constexpr int NUM_SOFTMAX_WARPS = 4 * NQ;
   static constexpr int TMA_WARP = NUM_SOFTMAX_WARPS;
   static constexpr int MMA_WARP = NUM_SOFTMAX_WARPS + 1;  // one MMA-issuing warp per tile: MMA_WARP + t
   static constexpr int THREADS = 32 * (NUM_SOFTMAX_WARPS + 1 + NQ);
-  // Each SM sub-partition owns a quarter of the register file and every
-  // fourth warp of the CTA, so the budget is 16384 / (32 * ceil(warps / 4)).
+  // Each SM sub-partition owns a quarter of the register file; the warps of
+  // all resident CTAs are spread over the four, so the budget is
+  // 16384 / (32 * ceil(warps per SM / 4)).  (Measured: two 6-warp CTAs at 168
+  // registers are resident together, although the occupancy API, which
+  // assumes warp w of every CTA sits on sub-partition w % 4, reports one.)
   static constexpr int WARPS_PER_SMSP = (CTAS_PER_SM * (NUM_SOFTMAX_WARPS + 1 + NQ) + 3) / 4;
   static constexpr int MAX_REGS = (16384 / (32 * WARPS_PER_SMSP)) / 8 * 8 > 255 ? 255
                                 : (16384 / (32 * WARPS_PER_SMSP)) / 8 * 8;
@@ -119,7 +136,15 @@ struct AttnCfg {
                                  : TMEM_USED <= 256 ? 256 : 512;
   static_assert(TMEM_USED <= 512, "TMEM budget");
   static constexpr int SMEM_TILES = NQ * Q_BYTES + (MLA_ONLY ? 1 : 2) * STAGES * KV_BYTES;
-  static constexpr int SMEM_BYTES = SMEM_TILES + 1024 /*barriers*/ + 1024 /*alignment*/;
+  // Two CTAs with three K/V stages need all but 1.5 KB of the SM's 228 KB, so
+  // they carry no alignment slack: the dynamic shared window of a kernel with
+  // no static shared memory starts 1024-byte aligned, which the kernel checks.
+#if defined(FMLM_TRACE) && FMLM_TRACE_SLOTS > 0
+  static constexpr int ALIGN_PAD = 1024;
+#else
+  static constexpr int ALIGN_PAD = (CTAS_PER_SM == 2) ? 0 : 1024;
+#endif
+  static constexpr int SMEM_BYTES = SMEM_TILES + 512 /*barriers*/ + ALIGN_PAD;
 };
 
 struct Seg {
@@ -165,7 +190,7 @@ __device__ __forceinline__ Item decode_item(const AttnParams& p, int w) {
     L = p.N;
     seq_start = 0;
   } else {
-    const int e = __ldg(p.work + 1 + r);
+    const int e = __ldg(p.work + kWorkHeader + r);
     b = e >> 16;
     pair = e & 0xFFFF;
     seq_start = __ldg(p.cu_q + b);
@@ -217,9 +242,12 @@ struct __align__(8) AttnBarriers {
   uint64_t k_full[4], v_full[4], kv_empty[4];
   uint64_t s_full[2], p_full[2], o_full[2], o_empty[2];
   uint64_t s_free[2], pv_done[2];  // separate-P pipeline only
+  uint64_t item_full[4], item_empty[4];  // ring of work-item indices, producer -> other roles
+  int item_idx[4];
   uint32_t tmem_base;
   int abort_flag;
 };
+static_assert(sizeof(AttnBarriers) <= 512, "barrier block is reserved 512 bytes");
 
 template <int D, int NQ, bool BF16>
 __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<D, NQ>::MAX_REGS))
@@ -238,6 +266,12 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
   };
 
   extern __shared__ uint8_t smem_raw[];
+  if constexpr (C::ALIGN_PAD == 0) {
+    if ((static_cast<uint32_t>(__cvta_generic_to_shared(smem_raw)) & 1023u) != 0) {
+      if (threadIdx.x == 0) atomicExch(p.err, kErrSmemAlign);
+      return;  // before any barrier, TMEM or TMA work
+    }
+  }
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;
   uint8_t* sK = sQ + NQ * C::Q_BYTES;
@@ -249,16 +283,22 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
   const int lane = threadIdx.x & 31;
   const bool mla = p.is_mla != 0;
 #ifdef FMLM_TRACE
+#if FMLM_TRACE_SLOTS > 0
   __shared__ unsigned long long tr_buf[4 * kTraceSlots];
   __shared__ int tr_cnt[4];
+#else
+  unsigned long long* tr_buf = nullptr;
+  int* tr_cnt = nullptr;
+#endif
   int tr_n = 0;
   int tr_role = -1;
-  if (p.trace && blockIdx.x == 0) {
+  if (kTraceSlots > 0 && p.trace && blockIdx.x == 0) {
     if (warp < C::NUM_SOFTMAX_WARPS && (threadIdx.x & 127) == 0) tr_role = warp >> 2;
     if (warp == C::TMA_WARP && lane == 0) tr_role = 2;
     if (warp == C::MMA_WARP && lane == 0) tr_role = 3;  // tile-0 MMA issuer
   }
-  if (threadIdx.x < 4 && p.trace) tr_cnt[threadIdx.x] = 0;
+  if (kTraceSlots > 0 && threadIdx.x < 4 && p.trace) tr_cnt[threadIdx.x] = 0;
+  const uint64_t tr_entry_ns = global_timer_ns();
 #endif
 
   if (threadIdx.x == 0) {
@@ -277,6 +317,10 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
       mbar_init(&bar->o_empty[t], 4);
       mbar_init(&bar->s_free[t], 4);
       mbar_init(&bar->pv_done[t], 1);
+    }
+    for (int i = 0; i < 4; ++i) {
+      mbar_init(&bar->item_full[i], 1);
+      mbar_init(&bar->item_empty[i], 5 * NQ);  // every MMA and softmax warp
     }
     bar->abort_flag = 0;
     mbar_fence_init();
@@ -307,11 +351,39 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
     atomicExch(p.err, kErrTimeout);
   };
 
+  // Next work item for the MMA and softmax warps (whole warp): the index the
+  // producer published in ring slot `ring`; num_items means no more work.
+  auto take_item = [&](uint32_t ring, int& w) -> bool {
+    if (failed) return false;
+    if (!mbar_wait(&bar->item_full[ring & 3], (ring >> 2) & 1u, abort_flag, tmo)) fail();
+    failed = __any_sync(0xffffffffu, failed);
+    if (failed) return false;
+    w = *reinterpret_cast<volatile int*>(&bar->item_idx[ring & 3]);
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&bar->item_empty[ring & 3]);
+    return w < num_items;
+  };
+
   if (warp == C::TMA_WARP) {
     // ------------------------------------------------------------ producer
     uint32_t q_empty_ph = 1, fix_ph = 0;
     uint32_t fill = 0;
-    for (int w = blockIdx.x; w < num_items && !failed; w += gridDim.x) {
+    // Work items are handed out dynamically: the first one is blockIdx.x, the
+    // rest come from a global counter (packed mode; the schedule is sorted by
+    // cost, so this is longest-first list scheduling), and each index is
+    // passed to the other roles through the item ring.
+    int w = blockIdx.x;
+    for (uint32_t ring = 0;; ++ring) {
+      if (!mbar_wait(&bar->item_empty[ring & 3], ((ring >> 2) & 1u) ^ 1u, abort_flag, tmo)) fail();
+      failed = __any_sync(0xffffffffu, failed);
+      if (failed) break;
+      if (lane == 0) {
+        bar->item_idx[ring & 3] = w;
+        mbar_arrive(&bar->item_full[ring & 3]);
+      }
+      if (w >= num_items) break;
+      int next = 0;
+      if (lane == 0) next = (p.mode == 0) ? w + (int)gridDim.x : (int)gridDim.x + atomicAdd(p.work + 1, 1);
       const Item it = decode_item<C::PAIR, BN, C::NDH>(p, w);
       // All lanes wait (a converged warp polls fastest); one lane issues.
       if (!mbar_wait(&bar->q_empty, q_empty_ph, abort_flag, tmo)) fail();
@@ -389,6 +461,7 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
           }
         }
       }
+      w = __shfl_sync(0xffffffffu, next, 0);
     }
   } else if (warp >= C::MMA_WARP) {
     // ------------------------------------------------------------ MMA issuers
@@ -442,7 +515,8 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
       return !failed;
     };
 
-    for (int w = blockIdx.x; w < num_items && !failed; w += gridDim.x) {
+    int w;
+    for (uint32_t ring = 0; take_item(ring, w); ++ring) {
       const Item it = decode_item<C::PAIR, BN, C::NDH>(p, w);
       const int nb = it.nblocks();
       if (!wait(&bar->q_full, q_full_ph)) break;
@@ -545,7 +619,8 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
     uint32_t s_ph = 0, o_ph = 0, pv_ph = 0;
     T* out = reinterpret_cast<T*>(p.out);
 
-    for (int w = blockIdx.x; w < num_items && !failed; w += gridDim.x) {
+    int w;
+    for (uint32_t ring = 0; take_item(ring, w); ++ring) {
       const Item it = decode_item<C::PAIR, BN, C::NDH>(p, w);
       const int nrows = it.qrows(t);
       if (nrows == 0) continue;
@@ -738,7 +813,14 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
   tc_fence_before();
   __syncthreads();
 #ifdef FMLM_TRACE
-  if (p.trace && blockIdx.x == 0) {
+  if (p.trace && threadIdx.x == 0) {
+    unsigned smid;
+    asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+    p.trace[8192 + 3 * blockIdx.x] = tr_entry_ns;
+    p.trace[8192 + 3 * blockIdx.x + 1] = global_timer_ns();
+    p.trace[8192 + 3 * blockIdx.x + 2] = smid;
+  }
+  if (kTraceSlots > 0 && p.trace && blockIdx.x == 0) {
     for (int r = 0; r < 4; ++r) {
       const int n = tr_cnt[r];
       if (threadIdx.x == 0) p.trace[r] = (unsigned long long)n;
@@ -746,6 +828,14 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
     }
   }
 #endif
+  if (p.mode == 1 && threadIdx.x == 0) {
+    // The last CTA to finish re-arms the item counter for the next launch.
+    __threadfence();
+    if (atomicAdd(p.work + 2, 1) == (int)gridDim.x - 1) {
+      atomicExch(p.work + 1, 0);
+      atomicExch(p.work + 2, 0);
+    }
+  }
   tc_fence_after();
   if (warp == C::MMA_WARP) {
     if (*abort_flag) {

@@ -166,13 +166,18 @@ __global__ void __launch_bounds__(kSchedThreads) sched_kernel(const int* __restr
     const int off = running;
     for (int i = 0; i < n; ++i) {
       const int idx = off + ex + i;
-      if (idx < cap) work[1 + idx] = (b << 16) | i;
+      if (idx < cap) work[kWorkHeader + idx] = (b << 16) | i;
     }
     __syncthreads();
     if (threadIdx.x == 0) running += total;
     __syncthreads();
   }
-  if (threadIdx.x == 0) work[0] = running < cap ? running : cap;
+  if (threadIdx.x == 0) {
+    work[0] = running < cap ? running : cap;
+    work[1] = 0;  // item counter and finished-CTA count of the attention kernel
+    work[2] = 0;
+    work[3] = 0;
+  }
 }
 
 int head_dim_supported(int d) { return d == 16 || d == 32 || d == 64 || d == 128 || d == 256 || d == 512; }
@@ -190,15 +195,20 @@ int launch_attn(const CUtensorMap* m, const AttnParams& p, long long items, cuda
   // Shared memory is padded so that exactly CTAS_PER_SM CTAs (TMEM owners)
   // fit on an SM: more would block in tcgen05.alloc.
   const int smem = C::CTAS_PER_SM == 1 ? std::max(C::SMEM_BYTES, 116 * 1024) : std::max(C::SMEM_BYTES, 80 * 1024);
-  const int grid = (int)std::min<long long>(items, (long long)device_sm_count() * C::CTAS_PER_SM);
   static bool configured[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !configured[dev]) {
+  if (dev < 0 || dev >= 64) return set_error(FMLM_ERR_CUDA, "device ordinal %d out of range", dev);
+  if (!configured[dev]) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return set_error(FMLM_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, (int)cudaSharedmemCarveoutMaxShared);
     if (e != cudaSuccess) return set_error(FMLM_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
     configured[dev] = true;
   }
+  // A persistent grid of CTAS_PER_SM CTAs per SM; items are handed out
+  // dynamically, so CTAs that cannot be resident at once only start late.
+  const int grid = (int)std::min<long long>(items, (long long)device_sm_count() * C::CTAS_PER_SM);
   kern<<<grid, C::THREADS, smem, s>>>(m[0], m[1], m[2], m[3], m[4], p);
   return check_launch("attn_fwd_kernel");
 }
@@ -285,7 +295,7 @@ extern "C" int fmlm_attn_dense_fwd(const fmlm_dense_args* a, void* stream) {
 extern "C" size_t fmlm_packed_workspace_bytes(int32_t batch, int64_t total_q_len, int32_t head_dim) {
   const int64_t pr = head_dim > 0 ? pair_rows(head_dim) : 128;
   const int64_t cap = total_q_len / pr + batch + 2;
-  return (size_t)((cap + 2) * sizeof(int32_t) + 15) / 16 * 16;
+  return (size_t)((cap + kWorkHeader) * sizeof(int32_t) + 15) / 16 * 16;
 }
 
 extern "C" int fmlm_attn_packed_fwd(const fmlm_packed_args* a, void* stream) {

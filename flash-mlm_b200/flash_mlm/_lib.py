@@ -190,14 +190,19 @@ def error_word(device: torch.device) -> torch.Tensor:
 
 
 def check_device_errors(device: torch.device | None = None) -> None:
-    """Synchronise and raise if any kernel on `device` reported a timeout."""
+    """Synchronise and raise if any kernel on `device` reported an error.
+
+    Codes: 1 = a bounded wait gave up; 2 = the dynamic shared-memory window
+    was not 1024-byte aligned (the kernel returned without touching memory).
+    """
     devs = [device] if device is not None else [torch.device("cuda", i) for i in list(_err_words)]
     for d in devs:
         w = error_word(d)
         v = int(w[0].item())
         if v != 0:
             w.zero_()
-            raise FlashMLMError(f"flash_mlm kernel on {d} gave up waiting (code {v}); results are invalid")
+            what = {1: "gave up waiting", 2: "found its shared memory misaligned"}.get(v, "failed")
+            raise FlashMLMError(f"flash_mlm kernel on {d} {what} (code {v}); results are invalid")
 
 
 def require_cuda(*tensors: torch.Tensor | None, what: str = "flash_mlm") -> None:

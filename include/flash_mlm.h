@@ -66,7 +66,7 @@ typedef struct fmlm_dense_args {
   fmlm_view4 q, k, v;         /* [B,H,N,D] */
   fmlm_view4 k_cache, v_cache;/* rows = context_len, heads = H (1 for MLA), batch = context_batch_size */
   void* out;                  /* [B,H,N,D] contiguous, dtype of q */
-  int32_t* error_word;        /* device int32; set non-zero if a kernel wait timed out */
+  int32_t* error_word;        /* device int32; kernels set 1 if a bounded wait gave up, 2 if shared memory was misaligned */
 } fmlm_dense_args;
 
 enum { FMLM_LAYOUT_PADDED = 0, FMLM_LAYOUT_PACKED = 1 };
