@@ -436,4 +436,28 @@ extern "C" int fmlm_attn_packed_fwd_noalloc(const fmlm_packed_args* a, void* str
 
 extern "C" const char* fmlm_last_error(void) { return last_error_slot().c_str(); }
 
+namespace fmlm {
+// One warp waits on a barrier whose phase never completes; the bounded wait
+// must return false, and the kernel reports it like the attention kernel does.
+__global__ void bounded_wait_probe_kernel(int* err, unsigned long long limit_ns) {
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    abort_flag = 0;
+    mbar_fence_init();
+  }
+  __syncthreads();
+  const bool ok = mbar_wait(&bar, 0, &abort_flag, limit_ns);
+  if (!ok && threadIdx.x == 0) atomicExch(err, kErrTimeout);
+}
+}  // namespace fmlm
+
+extern "C" int fmlm_selftest_bounded_wait(int32_t* error_word, uint64_t limit_ns, void* stream) {
+  if (!error_word) return set_error(FMLM_ERR_INVALID, "error_word is required");
+  if (limit_ns == 0 || limit_ns > 100000000ull) return set_error(FMLM_ERR_INVALID, "limit_ns must be in (0, 0.1 s]");
+  fmlm::bounded_wait_probe_kernel<<<1, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>(error_word, limit_ns);
+  return check_launch("bounded_wait_probe_kernel");
+}
+
 extern "C" int fmlm_version(void) { return 100; }

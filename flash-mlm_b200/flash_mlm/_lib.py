@@ -113,6 +113,8 @@ def lib() -> ctypes.CDLL:
         L.fmlm_attn_packed_fwd.restype = ctypes.c_int
         L.fmlm_attn_packed_fwd_noalloc.argtypes = [ctypes.POINTER(PackedArgs), vp]
         L.fmlm_attn_packed_fwd_noalloc.restype = ctypes.c_int
+        L.fmlm_selftest_bounded_wait.argtypes = [vp, ctypes.c_uint64, vp]
+        L.fmlm_selftest_bounded_wait.restype = ctypes.c_int
         L.fmlm_packed_workspace_bytes.argtypes = [i32, i64, i32]
         L.fmlm_packed_workspace_bytes.restype = ctypes.c_size_t
         L.fmlm_build_pack_metadata.argtypes = [vp, i32, i32, i32, vp, vp, vp, vp, vp, vp]

@@ -156,6 +156,12 @@ FMLM_API int fmlm_unpack_rows(const void* packed, int64_t total_tokens, int32_t 
 FMLM_API int fmlm_pad_packed_rows(const void* src, int64_t old_len, int64_t new_len, int32_t heads, int32_t head_dim,
                          int32_t elem_bytes, void* dst, void* stream);
 
+/* Self-test of the kernels' bounded waits (no counterpart in the reference):
+ * launches one CTA that waits on an mbarrier nobody arrives on, with the given
+ * limit.  The wait must give up and write 1 to *error_word (device int32);
+ * the GPU context stays usable.  Returns 0 if the launch succeeded. */
+FMLM_API int fmlm_selftest_bounded_wait(int32_t* error_word, uint64_t limit_ns, void* stream);
+
 /* Message of the last failed call on this thread ("" if none). */
 FMLM_API const char* fmlm_last_error(void);
 

@@ -5,6 +5,7 @@ Bars: metadata / pack / pad / unpack bit-exact; attention max-abs error
 <= 2e-3 (fp16) and <= 8e-3 (bf16) against fp32 math on the same rounded inputs.
 """
 
+import ctypes
 import math
 
 import numpy as np
@@ -499,3 +500,25 @@ def test_mla_latent512_dense_and_rejections():
     with pytest.raises(ValueError, match="HEAD_DIM must be one of"):
         fm().flash_attn_mlm(q.to(DEV), k.to(DEV), k.to(DEV), scale=0.05, is_mla=False)
     no_device_errors()
+
+
+@pytest.mark.gpu
+def test_bounded_wait_gives_up_and_context_stays_usable():
+    """A wait on a barrier nobody arrives on ends after its limit with an error
+    status; the context keeps working (a normal call afterwards is correct)."""
+    import time
+
+    from flash_mlm import _lib
+
+    dev = torch.device("cuda", 0)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    L = _lib.lib()
+    t0 = time.perf_counter()
+    assert L.fmlm_selftest_bounded_wait(ctypes.c_void_p(err.data_ptr()), 2_000_000, _lib.stream_ptr(dev)) == 0
+    torch.cuda.synchronize()
+    assert time.perf_counter() - t0 < 5.0
+    assert int(err.item()) == 1
+    q = torch.randn(1, 2, 64, 64, device=dev, dtype=torch.float16)
+    out = fm().flash_attn_mlm(q, q, q, scale=0.125)
+    ref = torch.softmax((q.float() @ q.float().transpose(-1, -2)) * 0.125, -1) @ q.float()
+    assert (out.float() - ref).abs().max().item() < 2e-3
