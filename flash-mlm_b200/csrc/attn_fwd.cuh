@@ -700,9 +700,6 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
               tc_fence_after();
             }
           }
-#ifndef FMLM_POLY_MODE
-#define FMLM_POLY_MODE 1  // measured: helps a little at D=64, hurts at D=128 (applied for D <= 64 only)
-#endif
           float sums[4] = {0.f, 0.f, 0.f, 0.f};
           // P in chunks of up to 32 packed columns (64 scores), each stored to
           // TMEM as soon as it is ready, so at most one chunk of packed P is live.
@@ -715,18 +712,8 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
               const int c = h0 + cc;
               const float x0 = fmaf(__uint_as_float(r[2 * c]), fac, neg_mu);
               const float x1 = fmaf(__uint_as_float(r[2 * c + 1]), fac, neg_mu);
-              // A share of the pairs (FMLM_POLY_MODE: 0 none, 1 one in four,
-              // 2 three in eight, 3 one in two) goes through the polynomial on
-              // the FMA pipe so the MUFU pipe (16 exp2 / clk / SM) is not the
-              // only limit.
-              const int k8 = c & 7;
-              const bool poly = D > 64                ? false
-                                : FMLM_POLY_MODE == 1 ? (c & 3) == 3
-                                : FMLM_POLY_MODE == 2 ? (k8 == 1 || k8 == 4 || k8 == 6)
-                                : FMLM_POLY_MODE == 3 ? (c & 1) == 1
-                                                      : false;
-              const float p0 = poly ? ex2_poly(x0) : ex2_approx(x0);
-              const float p1 = poly ? ex2_poly(x1) : ex2_approx(x1);
+              const float p0 = ex2_approx(x0);
+              const float p1 = ex2_approx(x1);
               sums[(2 * c) & 3] += p0;
               sums[(2 * c + 1) & 3] += p1;
               if constexpr (BF16) {

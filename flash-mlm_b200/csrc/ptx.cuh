@@ -204,21 +204,6 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
   return d;
 }
 
-// 2^x on the FMA/ALU pipes (no MUFU): x = j + f with j = round(x) read from
-// the low mantissa bits of x + 1.5*2^23, 2^f on [-0.5, 0.5] by a degree-3
-// polynomial fitted for minimum relative error (max 7.5e-5, below the
-// f16/bf16 rounding applied to P), and j added to the exponent field.
-// Inputs below -126 are clamped (results ~1e-38 instead of 0).
-__device__ __forceinline__ float ex2_poly(float x) {
-  x = fmaxf(x, -126.0f);
-  const float t = x + 12582912.0f;
-  const float fr = x - (t - 12582912.0f);
-  float p = fmaf(0.05517132207751274f, fr, 0.24261054396629333f);
-  p = fmaf(p, fr, 0.6932609677314758f);
-  p = fmaf(p, fr, 0.9999281167984009f);
-  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
-}
-
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
