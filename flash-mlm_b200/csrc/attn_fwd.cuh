@@ -71,7 +71,10 @@ struct AttnParams {
 #endif
 // FMLM_TRACE_SLOTS = 0 records only per-CTA entry/exit times (no static
 // shared memory, so the occupancy is that of the product build).
-constexpr int kTraceSlots = FMLM_TRACE_SLOTS;
+// FMLM_TRACE_SLOTS < 0 writes the records straight to global memory (1024
+// per role), also without static shared memory.
+constexpr bool kTraceGlobal = FMLM_TRACE_SLOTS < 0;
+constexpr int kTraceSlots = kTraceGlobal ? 1024 : FMLM_TRACE_SLOTS;
 #define FMLM_TR(ev)                                                                                   \
   do {                                                                                                \
     if (tr_role >= 0 && tr_n < kTraceSlots)                                                           \
@@ -287,7 +290,7 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
   __shared__ unsigned long long tr_buf[4 * kTraceSlots];
   __shared__ int tr_cnt[4];
 #else
-  unsigned long long* tr_buf = nullptr;
+  unsigned long long* tr_buf = kTraceGlobal && p.trace ? p.trace + 4 : nullptr;
   int* tr_cnt = nullptr;
 #endif
   int tr_n = 0;
@@ -297,7 +300,7 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
     if (warp == C::TMA_WARP && lane == 0) tr_role = 2;
     if (warp == C::MMA_WARP && lane == 0) tr_role = 3;  // tile-0 MMA issuer
   }
-  if (kTraceSlots > 0 && threadIdx.x < 4 && p.trace) tr_cnt[threadIdx.x] = 0;
+  if (!kTraceGlobal && kTraceSlots > 0 && threadIdx.x < 4 && p.trace) tr_cnt[threadIdx.x] = 0;
   const uint64_t tr_entry_ns = global_timer_ns();
 #endif
 
@@ -795,7 +798,10 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
 
   // ------------------------------------------------------------ teardown
 #ifdef FMLM_TRACE
-  if (tr_role >= 0) tr_cnt[tr_role] = tr_n;
+  if (tr_role >= 0) {
+    if (kTraceGlobal) p.trace[tr_role] = tr_n;
+    else tr_cnt[tr_role] = tr_n;
+  }
 #endif
   tc_fence_before();
   __syncthreads();
@@ -807,7 +813,7 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
     p.trace[8192 + 3 * blockIdx.x + 1] = global_timer_ns();
     p.trace[8192 + 3 * blockIdx.x + 2] = smid;
   }
-  if (kTraceSlots > 0 && p.trace && blockIdx.x == 0) {
+  if (!kTraceGlobal && kTraceSlots > 0 && p.trace && blockIdx.x == 0) {
     for (int r = 0; r < 4; ++r) {
       const int n = tr_cnt[r];
       if (threadIdx.x == 0) p.trace[r] = (unsigned long long)n;
