@@ -496,7 +496,7 @@ def main():
         else:
             gbs = alg_bytes / (kernel_ms * 1e-3) / 1e9
             roof = {"bound": "hbm", "achieved": gbs, "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": gbs / pk["hbm_gbs"]}
-        roof.update({"traffic": traffic, "kernel": f"attn_fwd_kernel<{w.D},{1 if w.D >= 256 else 2},"
+        roof.update({"traffic": traffic, "kernel": f"attn_fwd_kernel<{w.D},{1 if w.D >= 256 or w.D == 64 else 2},"
                      f"{'bf16' if w.dtype == torch.bfloat16 else 'f16'}>", "kernel_ms": kernel_ms,
                      "alg_flops_per_launch": k_flops, "alg_bytes_per_launch": alg_bytes,
                      "roofline_ms": max(t_tensor, t_hbm) * 1e3,

@@ -116,7 +116,16 @@ struct AttnCfg {
 #ifndef FMLM_STAGES_2CTA
 #define FMLM_STAGES_2CTA 3
 #endif
-  static constexpr int STAGES = (CTAS_PER_SM == 2) ? FMLM_STAGES_2CTA : (D <= 32) ? 4 : (D <= 64) ? 3 : (D == 512) ? 3
+#ifndef FMLM_EARLY_O
+#define FMLM_EARLY_O 1
+#endif
+#ifndef FMLM_QBUF_2CTA
+#define FMLM_QBUF_2CTA 1
+#endif
+  // Q buffers: with two, the next item's Q is loaded while the current item
+  // still computes, so its first S is ready when the softmax reaches it.
+  static constexpr int QBUF = (CTAS_PER_SM == 2) ? FMLM_QBUF_2CTA : 1;
+  static constexpr int STAGES = (CTAS_PER_SM == 2) ? (QBUF == 2 ? 2 : FMLM_STAGES_2CTA) : (D <= 32) ? 4 : (D <= 64) ? 3 : (D == 512) ? 3
                               : (D == 128 && BN == 64) ? 4 : 2;
   static constexpr int NUM_SOFTMAX_WARPS = 4 * NQ;
   static constexpr int TMA_WARP = NUM_SOFTMAX_WARPS;
@@ -141,7 +150,7 @@ struct AttnCfg {
   static constexpr int TMEM_COLS = TMEM_USED <= 32 ? 32 : TMEM_USED <= 64 ? 64 : TMEM_USED <= 128 ? 128
                                  : TMEM_USED <= 256 ? 256 : 512;
   static_assert(TMEM_USED <= 512, "TMEM budget");
-  static constexpr int SMEM_TILES = NQ * Q_BYTES + (MLA_ONLY ? 1 : 2) * STAGES * KV_BYTES;
+  static constexpr int SMEM_TILES = QBUF * NQ * Q_BYTES + (MLA_ONLY ? 1 : 2) * STAGES * KV_BYTES;
   // Two CTAs with three K/V stages need all but 1.5 KB of the SM's 228 KB, so
   // they carry no alignment slack: the dynamic shared window of a kernel with
   // no static shared memory starts 1024-byte aligned, which the kernel checks.
@@ -150,7 +159,8 @@ struct AttnCfg {
 #else
   static constexpr int ALIGN_PAD = (CTAS_PER_SM == 2) ? 0 : 1024;
 #endif
-  static constexpr int SMEM_BYTES = SMEM_TILES + 512 /*barriers*/ + ALIGN_PAD;
+  static constexpr int ITEM_RING_BYTES = 4 * 96;  // decoded work items passed producer -> consumers
+  static constexpr int SMEM_BYTES = SMEM_TILES + 512 /*barriers*/ + ITEM_RING_BYTES + ALIGN_PAD;
 };
 
 struct Seg {
@@ -243,8 +253,10 @@ __device__ __forceinline__ Item decode_item(const AttnParams& p, int w) {
   return it;
 }
 
+static_assert(sizeof(Item) <= 96, "item ring slot");
+
 struct __align__(8) AttnBarriers {
-  uint64_t q_full, q_empty, fix;
+  uint64_t q_full[2], q_empty[2], fix;
   uint64_t k_full[4], v_full[4], kv_empty[4];
   uint64_t s_full[2], p_full[2], o_full[2], o_empty[2];
   uint64_t s_free[2], pv_done[2];  // separate-P pipeline only
@@ -281,10 +293,11 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
   }
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;
-  uint8_t* sK = sQ + NQ * C::Q_BYTES;
+  uint8_t* sK = sQ + C::QBUF * NQ * C::Q_BYTES;
   uint8_t* sV = C::MLA_ONLY ? sK : sK + STAGES * C::KV_BYTES;
   AttnBarriers* bar = reinterpret_cast<AttnBarriers*>(sV + STAGES * C::KV_BYTES);
   volatile int* abort_flag = &bar->abort_flag;
+  Item* item_ring = reinterpret_cast<Item*>(reinterpret_cast<uint8_t*>(bar) + 512);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -309,8 +322,10 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
 #endif
 
   if (threadIdx.x == 0) {
-    mbar_init(&bar->q_full, 1);
-    mbar_init(&bar->q_empty, NQ);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bar->q_full[i], 1);
+      mbar_init(&bar->q_empty[i], NQ);
+    }
     mbar_init(&bar->fix, 1);
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&bar->k_full[s], 1);
@@ -362,12 +377,15 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
 
   // Next work item for the MMA and softmax warps (whole warp): the index the
   // producer published in ring slot `ring`; num_items means no more work.
-  auto take_item = [&](uint32_t ring, int& w) -> bool {
+  // The producer also publishes the decoded item, so consumers do not repeat
+  // decode_item's dependent global loads at every item start.
+  auto take_item = [&](uint32_t ring, int& w, Item& it) -> bool {
     if (failed) return false;
     if (!mbar_wait(&bar->item_full[ring & 3], (ring >> 2) & 1u, abort_flag, tmo)) fail();
     failed = __any_sync(0xffffffffu, failed);
     if (failed) return false;
     w = *reinterpret_cast<volatile int*>(&bar->item_idx[ring & 3]);
+    if (w < num_items) it = item_ring[ring & 3];
     __syncwarp();
     if (lane == 0) mbar_arrive(&bar->item_empty[ring & 3]);
     return w < num_items;
@@ -375,44 +393,85 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
 
   if (warp == C::TMA_WARP) {
     // ------------------------------------------------------------ producer
-    uint32_t q_empty_ph = 1, fix_ph = 0;
+    uint32_t fix_ph = 0;
+    // A partial last block of a padded main segment: rows [valid, BN) of its V
+    // tile (K for MLA) hold the caller's padding, which may be non-finite; P is
+    // zero there but 0 * NaN is not, so they are cleared once the tile lands.
+    // The clearing is deferred to just before the producer's next wait for a
+    // free K/V stage (the only wait that can depend on this tile), so the next
+    // item's Q and first blocks are requested without waiting for it.
+    uint8_t* pend_tile = nullptr;
+    int pend_valid = 0;
+    uint64_t* pend_bar = nullptr;
+    auto resolve_fix = [&]() {
+      if (pend_tile == nullptr || failed) return;
+      if (!mbar_wait(&bar->fix, fix_ph, abort_flag, tmo)) fail();
+      fix_ph ^= 1u;
+      failed = __any_sync(0xffffffffu, failed);
+      if (!failed) {
+        const int nbytes = (BN - pend_valid) * SWB;
+        for (int s = 0; s < C::NSLAB; ++s) {
+          uint4* z = reinterpret_cast<uint4*>(pend_tile + s * (BN * SWB) + pend_valid * SWB);
+          for (int i = lane; i < nbytes / 16; i += 32) z[i] = make_uint4(0, 0, 0, 0);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(pend_bar);
+      }
+      pend_tile = nullptr;
+    };
     uint32_t fill = 0;
     // Work items are handed out dynamically: the first one is blockIdx.x, the
     // rest come from a global counter (packed mode; the schedule is sorted by
     // cost, so this is longest-first list scheduling), and each index is
     // passed to the other roles through the item ring.
+    auto issue_q = [&](const Item& q_it, int qs) {
+      if (lane == 0) {
+        FMLM_TR(42);
+        const uint32_t nq = (q_it.qrows0 > 0 ? 1u : 0u) + (NQ > 1 && q_it.qrows1 > 0 ? 1u : 0u);
+        mbar_arrive_expect_tx(&bar->q_full[qs], nq * C::Q_BYTES);
+#pragma unroll
+        for (int t = 0; t < NQ; ++t) {
+          if (q_it.qrows(t) == 0) continue;
+          for (int s = 0; s < C::NSLAB; ++s)
+            tma_load_4d(sQ + (qs * NQ + t) * C::Q_BYTES + s * (BM * SWB), &tm_q, &bar->q_full[qs], s * C::SLAB_COLS,
+                        q_it.qrow0 + t * BM, q_it.qh, q_it.qb);
+        }
+      }
+      __syncwarp();
+    };
+    bool q_pre = false;
+    Item cur;
+    bool have_cur = false;  // cur holds the decoded item w (decoded during the previous item)
     int w = blockIdx.x;
     for (uint32_t ring = 0;; ++ring) {
       if (!mbar_wait(&bar->item_empty[ring & 3], ((ring >> 2) & 1u) ^ 1u, abort_flag, tmo)) fail();
       failed = __any_sync(0xffffffffu, failed);
       if (failed) break;
+      const Item it = (w < num_items) ? (have_cur ? cur : decode_item<C::PAIR, BN, C::NDH>(p, w)) : Item{};
       if (lane == 0) {
+        if (w < num_items) item_ring[ring & 3] = it;
         bar->item_idx[ring & 3] = w;
         mbar_arrive(&bar->item_full[ring & 3]);
       }
       if (w >= num_items) break;
       int next = 0;
       if (lane == 0) next = (p.mode == 0) ? w + (int)gridDim.x : (int)gridDim.x + atomicAdd(p.work + 1, 1);
-      const Item it = decode_item<C::PAIR, BN, C::NDH>(p, w);
-      // All lanes wait (a converged warp polls fastest); one lane issues.
-      if (!mbar_wait(&bar->q_empty, q_empty_ph, abort_flag, tmo)) fail();
-      failed = __any_sync(0xffffffffu, failed);
-      q_empty_ph ^= 1;
-      if (lane == 0) {
-        FMLM_TR(42);
-        if (!failed) {
-          const uint32_t nq = (it.qrows0 > 0 ? 1u : 0u) + (NQ > 1 && it.qrows1 > 0 ? 1u : 0u);
-          mbar_arrive_expect_tx(&bar->q_full, nq * C::Q_BYTES);
-#pragma unroll
-          for (int t = 0; t < NQ; ++t) {
-            if (it.qrows(t) == 0) continue;
-            for (int s = 0; s < C::NSLAB; ++s)
-              tma_load_4d(sQ + t * C::Q_BYTES + s * (BM * SWB), &tm_q, &bar->q_full, s * C::SLAB_COLS,
-                          it.qrow0 + t * BM, it.qh, it.qb);
-          }
-        }
+      next = __shfl_sync(0xffffffffu, next, 0);
+      // Q buffer ring % QBUF, used for the (ring / QBUF)-th time.  With two
+      // buffers the next item's Q is requested during this item, as soon as
+      // its buffer is free (q_pre), so it has landed when this item ends.
+      if (!q_pre) {
+        const int qs = ring % C::QBUF;
+        if (!mbar_wait(&bar->q_empty[qs], ((ring / C::QBUF) & 1u) ^ 1u, abort_flag, tmo)) fail();
+        failed = __any_sync(0xffffffffu, failed);
+        if (!failed) issue_q(it, qs);
       }
-      failed = __shfl_sync(0xffffffffu, failed, 0);
+      q_pre = false;
+      const bool want_next = C::QBUF == 2 && next < num_items;
+      const int qn = (ring + 1) % C::QBUF;
+      const uint32_t qn_par = (((ring + 1) / C::QBUF) & 1u) ^ 1u;
+      const Item itn = (next < num_items) ? decode_item<C::PAIR, BN, C::NDH>(p, next) : it;
       const int nb = it.nblocks();
       for (int j = 0; j < nb && !failed; ++j, ++fill) {
         {
@@ -426,6 +485,7 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
           const bool fix = sgm.fix && valid < BN;
           uint8_t* tk = sK + st * C::KV_BYTES;
           uint8_t* tv = sV + st * C::KV_BYTES;
+          resolve_fix();
           if (!mbar_wait(&bar->kv_empty[st], ph ^ 1u, abort_flag, tmo)) fail();
           failed = __any_sync(0xffffffffu, failed);
           if (lane == 0) {
@@ -450,28 +510,26 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
             }
           }
           failed = __shfl_sync(0xffffffffu, failed, 0);
-          if (fix && !failed) {
-            // Rows [valid, BN) of this V tile hold the caller's padding, which
-            // may be non-finite; P is zero there but 0 * NaN is not, so clear them.
-            if (!mbar_wait(&bar->fix, fix_ph, abort_flag, tmo)) fail();
-            fix_ph ^= 1u;
-            failed = __any_sync(0xffffffffu, failed);
-            if (!failed) {
-              uint8_t* tf = mla ? tk : tv;
-              const int nbytes = (BN - valid) * SWB;
-              for (int s = 0; s < C::NSLAB; ++s) {
-                uint4* z = reinterpret_cast<uint4*>(tf + s * (BN * SWB) + valid * SWB);
-                for (int i = lane; i < nbytes / 16; i += 32) z[i] = make_uint4(0, 0, 0, 0);
-              }
-              fence_proxy_async_smem();
-              __syncwarp();
-              if (lane == 0) mbar_arrive(mla ? &bar->k_full[st] : &bar->v_full[st]);
+          if (want_next && !q_pre && !failed) {
+            bool ready = false;
+            if (lane == 0) ready = mbar_test_wait(smem_u32(&bar->q_empty[qn]), qn_par);
+            if (__shfl_sync(0xffffffffu, ready, 0)) {
+              issue_q(itn, qn);
+              q_pre = true;
             }
+          }
+          if (fix && !failed) {
+            pend_tile = mla ? tk : tv;
+            pend_valid = valid;
+            pend_bar = mla ? &bar->k_full[st] : &bar->v_full[st];
           }
         }
       }
-      w = __shfl_sync(0xffffffffu, next, 0);
+      w = next;
+      cur = itn;
+      have_cur = next < num_items;
     }
+    resolve_fix();
   } else if (warp >= C::MMA_WARP) {
     // ------------------------------------------------------------ MMA issuers
     // Warp MMA_WARP + t issues every tcgen05.mma of query tile t, so the two
@@ -483,12 +541,13 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
     constexpr uint32_t idesc_qk = make_idesc_f16(fmt, 0, 0, BM, BN);
     constexpr uint32_t idesc_pv = make_idesc_f16(fmt, 0, 1, BM, C::DV);
     constexpr uint32_t layout = swizzle_code(SWB);
-    const uint32_t sQa = smem_u32(sQ) + t * C::Q_BYTES, sKa = smem_u32(sK), sVa = smem_u32(sV);
+    const uint32_t sQ0 = smem_u32(sQ) + t * C::Q_BYTES, sKa = smem_u32(sK), sVa = smem_u32(sV);
+    uint32_t sQa = sQ0;  // this item's Q buffer
     const uint32_t tS_d = tmem_base + C::TM_S + t * BN;
     const uint32_t tO_d = tmem_base + C::TM_O + t * C::DV;
     const uint32_t tP_a = tmem_base + (C::SEP_P ? C::TM_P + t * (BN / 2) : C::TM_S + t * BN);
     const bool leader = elect_one();
-    uint32_t q_full_ph = 0, p_ph = 0, o_empty_ph = 1, s_free_ph = 0;
+    uint32_t p_ph = 0, o_empty_ph = 1, s_free_ph = 0;
     bool first_item = true;
     uint32_t fill = 0;
 
@@ -525,16 +584,18 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
     };
 
     int w;
-    for (uint32_t ring = 0; take_item(ring, w); ++ring) {
-      const Item it = decode_item<C::PAIR, BN, C::NDH>(p, w);
+    Item it;
+    for (uint32_t ring = 0; take_item(ring, w, it); ++ring) {
       const int nb = it.nblocks();
-      if (!wait(&bar->q_full, q_full_ph)) break;
-      q_full_ph ^= 1u;
+      const int qs = ring % C::QBUF;
+      uint64_t* q_empty = &bar->q_empty[qs];
+      sQa = sQ0 + qs * NQ * C::Q_BYTES;
+      if (!wait(&bar->q_full[qs], (ring / C::QBUF) & 1u)) break;
       if (t == 0) FMLM_TR(34);
       if (it.qrows(t) == 0) {
         // This tile is empty for the item: release Q and every K/V stage in
         // order (after each fill has landed, so no release runs ahead).
-        if (leader) mbar_arrive(&bar->q_empty);
+        if (leader) mbar_arrive(q_empty);
         for (int j = 0; j < nb; ++j) {
           const int st = (fill + j) % STAGES;
           if (!wait(&bar->k_full[st], ((fill + j) / STAGES) & 1u)) break;
@@ -555,7 +616,7 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
         tc_fence_after();
         issue_s(st);
         commit(&bar->s_full[t]);
-        if (nb == 1) commit(&bar->q_empty);
+        if (nb == 1) commit(q_empty);
       }
       for (int j = 0; j < nb && !failed; ++j) {
         const int st = (fill + j) % STAGES;
@@ -572,7 +633,7 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
             issue_s(st1);
             commit(&bar->s_full[t]);
             if (t == 0) FMLM_TR(32);
-            if (j + 2 == nb) commit(&bar->q_empty);
+            if (j + 2 == nb) commit(q_empty);
           }
           // ... then O_t += P_t(j) V(j) once P_t(j) is in TMEM.
           if (!mla && !wait(&bar->v_full[st], ph)) break;
@@ -607,7 +668,7 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
           } else {
             commit(&bar->o_full[t]);
           }
-          if (j + 2 == nb) commit(&bar->q_empty);
+          if (j + 2 == nb) commit(q_empty);
           commit(&bar->kv_empty[st]);
         }
       }
@@ -636,8 +697,8 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
     if (kPingPong && t == 1 && lane == 0) mbar_arrive(&bar->exp_tok[0]);
 
     int w;
-    for (uint32_t ring = 0; take_item(ring, w); ++ring) {
-      const Item it = decode_item<C::PAIR, BN, C::NDH>(p, w);
+    Item it;
+    for (uint32_t ring = 0; take_item(ring, w, it); ++ring) {
       const int nrows = it.qrows(t);
       if (nrows == 0) continue;
       const bool row_valid = row < nrows;
@@ -791,31 +852,46 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
       tc_fence_after();
       const float inv = (l > 0.f) ? 1.0f / l : 1.0f;
       T* orow = out + (it.out_row0 + t * BM + row) * (long long)D + it.dh * C::DV;
-#pragma unroll 4
-      for (int c0 = 0; c0 < C::DV; c0 += OC) {
-        uint32_t o[OC];
-        tmem_ld_chunk(tO + c0, o);
-        if (row_valid) {
-          uint32_t v[OC / 2];
+      auto store_chunk = [&](const uint32_t(&o)[OC], int c0) {
+        if (!row_valid) return;
+        uint32_t v[OC / 2];
 #pragma unroll
-          for (int c = 0; c < OC / 2; ++c) {
-            const float a = __uint_as_float(o[2 * c]) * inv, b = __uint_as_float(o[2 * c + 1]) * inv;
-            if constexpr (BF16) {
-              __nv_bfloat162 v2 = __floats2bfloat162_rn(a, b);
-              v[c] = *reinterpret_cast<uint32_t*>(&v2);
-            } else {
-              __half2 v2 = __floats2half2_rn(a, b);
-              v[c] = *reinterpret_cast<uint32_t*>(&v2);
-            }
+        for (int c = 0; c < OC / 2; ++c) {
+          const float a = __uint_as_float(o[2 * c]) * inv, b = __uint_as_float(o[2 * c + 1]) * inv;
+          if constexpr (BF16) {
+            __nv_bfloat162 v2 = __floats2bfloat162_rn(a, b);
+            v[c] = *reinterpret_cast<uint32_t*>(&v2);
+          } else {
+            __half2 v2 = __floats2half2_rn(a, b);
+            v[c] = *reinterpret_cast<uint32_t*>(&v2);
           }
-          uint4* dst = reinterpret_cast<uint4*>(orow + c0);
-#pragma unroll
-          for (int q = 0; q < OC / 8; ++q) dst[q] = make_uint4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
         }
+        uint4* dst = reinterpret_cast<uint4*>(orow + c0);
+#pragma unroll
+        for (int q = 0; q < OC / 8; ++q) dst[q] = make_uint4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+      };
+      if constexpr (C::DV <= 64 && FMLM_EARLY_O) {
+        // Small O: read all of it, hand TMEM back to the MMA warp (the next
+        // item's first PV may start), then normalise and store.
+        uint32_t o[C::DV / OC][OC];
+#pragma unroll
+        for (int k = 0; k < C::DV / OC; ++k) tmem_ld_chunk(tO + k * OC, o[k]);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bar->o_empty[t]);
+#pragma unroll
+        for (int k = 0; k < C::DV / OC; ++k) store_chunk(o[k], k * OC);
+      } else {
+#pragma unroll 4
+        for (int c0 = 0; c0 < C::DV; c0 += OC) {
+          uint32_t o[OC];
+          tmem_ld_chunk(tO + c0, o);
+          store_chunk(o, c0);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bar->o_empty[t]);
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bar->o_empty[t]);
       FMLM_TR(20 + t);
     }
   }

@@ -226,10 +226,18 @@ int dispatch(int D, const CUtensorMap* m, const AttnParams& p, long long items, 
   }
 }
 
-#ifndef FMLM_BN_D128
-#define FMLM_BN_D128 128
-#endif
-int kv_box_rows(int D) { return D == 512 ? 32 : D >= 256 ? 64 : D == 128 ? FMLM_BN_D128 : 128; }
+// K/V tensor-map box height = the kernel's key block (AttnCfg::BN) for the
+// instantiation dispatch() launches, so the two cannot disagree.
+int kv_box_rows(int D) {
+  switch (D) {
+    case 16: return AttnCfg<16, 2>::BN;
+    case 32: return AttnCfg<32, 2>::BN;
+    case 64: return AttnCfg<64, FMLM_NQ_D64>::BN;
+    case 128: return AttnCfg<128, 2>::BN;
+    case 256: return AttnCfg<256, 1>::BN;
+    default: return AttnCfg<512, 1>::BN;
+  }
+}
 int o_halves(int D) { return D == 512 ? 2 : 1; }
 
 constexpr unsigned long long kTimeoutNs = 2000000000ull;  // 2 s per wait
