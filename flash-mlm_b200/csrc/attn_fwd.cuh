@@ -397,9 +397,9 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
     // A partial last block of a padded main segment: rows [valid, BN) of its V
     // tile (K for MLA) hold the caller's padding, which may be non-finite; P is
     // zero there but 0 * NaN is not, so they are cleared once the tile lands.
-    // The clearing is deferred to just before the producer's next wait for a
-    // free K/V stage (the only wait that can depend on this tile), so the next
-    // item's Q and first blocks are requested without waiting for it.
+    // For a V tile the clearing is deferred to just before the producer's next
+    // wait for a free K/V stage (the only wait that can depend on V), so the
+    // next item's Q and first blocks are requested without waiting for it.
     uint8_t* pend_tile = nullptr;
     int pend_valid = 0;
     uint64_t* pend_bar = nullptr;
@@ -522,6 +522,9 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
             pend_tile = mla ? tk : tv;
             pend_valid = valid;
             pend_bar = mla ? &bar->k_full[st] : &bar->v_full[st];
+            // With MLA the cleared tile is K, which this item's last S (and so
+            // the release of the Q buffer the next item waits for) needs.
+            if (mla) resolve_fix();
           }
         }
       }

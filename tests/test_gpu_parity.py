@@ -462,10 +462,13 @@ def test_large_logits_rescale_path():
 # ----------------------------------------------------------------- MLA with a 512-wide latent (no reference counterpart)
 
 
+# H=64 gives more work items than CTAs, so CTAs run several items back to back,
+# each ending on a partial key block whose caller padding is cleared in shared memory.
+@pytest.mark.parametrize("H", [4, 64])
 @pytest.mark.parametrize("causal", [False, True])
-def test_mla_latent512_compressed_vs_oracle(causal):
-    g = torch.Generator().manual_seed(512 + causal)
-    B, H, N, D = 3, 4, 70, 512
+def test_mla_latent512_compressed_vs_oracle(causal, H):
+    g = torch.Generator().manual_seed(512 + causal + H)
+    B, N, D = 3, 70, 512
     lengths = torch.tensor([70, 5, 41], dtype=torch.int32)
     q = (_rand((B, H, N, D), torch.bfloat16, g, 0.5))
     k = (_rand((B, 1, N, D), torch.bfloat16, g, 0.5)).expand(B, H, N, D)
