@@ -459,6 +459,39 @@ def test_large_logits_rescale_path():
     no_device_errors()
 
 
+# ----------------------------------------------------------------- long per-sequence contexts
+# Few work items, each walking a long context (up to 47 key blocks) then its
+# own tokens; two identical calls must give bit-identical outputs.
+
+
+@pytest.mark.parametrize("D,dt", [(64, torch.bfloat16), (64, torch.float16), (128, torch.bfloat16), (256, torch.float16)])
+def test_long_context_vs_oracle_and_repeatable(D, dt):
+    g = torch.Generator().manual_seed(900 + D)
+    B, H, N = 3, 2, 300
+    lengths = torch.tensor([300, 7, 170], dtype=torch.int32)
+    q, k, v = (_rand((B, H, N, D), dt, g) for _ in range(3))
+    ctx = torch.tensor([3000, 129, 1500], dtype=torch.int32)
+    cu_kv = torch.cat([torch.zeros(1, dtype=torch.int32), ctx.cumsum(0).to(torch.int32)])
+    tcl = int(cu_kv[-1])
+    kc, vc = (_rand((H * tcl, D), dt, g) for _ in range(2))
+    scale = D ** -0.5
+    cache = fm().InferenceCache()
+    cache.prefill_kv_cache(0, k_cache=kc.to(DEV), v_cache=vc.to(DEV), total_context_len=tcl,
+                           cu_seqlens_kv=cu_kv.to(DEV), context_batch_size=B, is_mla=False, num_heads=H, head_dim=D)
+    meta = fm().build_pack_metadata(lengths.to(DEV), N, 64)
+    out = fm().flash_attn_mlm_compressed(q.to(DEV), k.to(DEV), v.to(DEV), num_heads=H, q_meta=meta, scale=scale,
+                                         inference_cache=cache, layer_id=0, block_n=64)
+    out2 = fm().flash_attn_mlm_compressed(q.to(DEV), k.to(DEV), v.to(DEV), num_heads=H, q_meta=meta, scale=scale,
+                                          inference_cache=cache, layer_id=0, block_n=64)
+    ref = oracle.attention_packed(q.float().numpy(), k.float().numpy(), v.float().numpy(),
+                                  meta.cu_seqlens.cpu().numpy(), scale, k_cache=kc.float().numpy(),
+                                  v_cache=vc.float().numpy(), cu_kv=cu_kv.numpy(), context_batch_size=B,
+                                  total_context_len=tcl)
+    assert_close_tol(out, ref, dt, f"long context D={D}")
+    assert torch.equal(out, out2)
+    no_device_errors()
+
+
 # ----------------------------------------------------------------- MLA with a 512-wide latent (no reference counterpart)
 
 
