@@ -104,57 +104,94 @@ template <> struct VecT<4> { using T = uint32_t; };
 template <> struct VecT<2> { using T = uint16_t; };
 template <> struct VecT<1> { using T = uint8_t; };
 
-__device__ __forceinline__ int find_seq(const int* __restrict__ cu, int B, long long r) {
-  int lo = 0, hi = B - 1;  // largest b with cu[b] <= r
-  while (lo < hi) {
-    const int mid = (lo + hi + 1) >> 1;
-    if (cu[mid] <= r) lo = mid; else hi = mid - 1;
-  }
-  return lo;
-}
+// Row copies are organised per (row chunk, head, sequence): grid
+// (ceil(rows / kRowsPerCta), H, B [+1]), so a CTA copies up to kRowsPerCta
+// consecutive rows of one sequence and head with no per-element search or
+// 64-bit division, and each thread issues kUnroll loads before its stores.
+constexpr int kRowsPerCta = 64;
+constexpr int kCopyThreads = 256;
+constexpr int kUnroll = 4;
 
 // out[h][r] = x[b(r)][h][r - cu[b(r)]] for r < total_tokens, zero for r < total_padded.
+// Sequence slice b = B of the grid writes the zero rows [total_tokens, total_padded).
 template <int V>
-__global__ void pack_rows_kernel(const uint8_t* __restrict__ x, long long sb, long long sh, long long sr,
-                                 int row_bytes, int H, const int* __restrict__ cu, int B, long long total_tokens,
-                                 long long total_padded, uint8_t* __restrict__ out) {
+__global__ void __launch_bounds__(kCopyThreads) pack_rows_kernel(const uint8_t* __restrict__ x, long long sb,
+                                                                 long long sh, long long sr, int row_bytes,
+                                                                 const int* __restrict__ cu, int B,
+                                                                 long long total_tokens, long long total_padded,
+                                                                 uint8_t* __restrict__ out) {
   using T = typename VecT<V>::T;
   const int nvec = row_bytes / V;
-  const long long n = (long long)H * total_padded * nvec;
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
-    const long long row = i / nvec;
-    const int v = (int)(i - row * nvec);
-    const int h = (int)(row / total_padded);
-    const long long r = row - (long long)h * total_padded;
-    T val{};
-    if (r < total_tokens) {
-      const int b = find_seq(cu, B, r);
-      const long long t = r - cu[b];
-      val = *reinterpret_cast<const T*>(x + b * sb + h * sh + t * sr + (long long)v * V);
+  const int h = blockIdx.y;
+  const long long r0 = (long long)blockIdx.x * kRowsPerCta;
+  for (int b = blockIdx.z; b <= B; b += gridDim.z) {
+    long long len, dst0;
+    const uint8_t* src = nullptr;
+    if (b < B) {
+      const int s0 = __ldg(cu + b);
+      len = __ldg(cu + b + 1) - s0;
+      dst0 = (long long)h * total_padded + s0;
+      src = x + b * sb + h * sh;
+    } else {
+      len = total_padded - total_tokens;
+      dst0 = (long long)h * total_padded + total_tokens;
     }
-    *reinterpret_cast<T*>(out + row * row_bytes + (long long)v * V) = val;
+    if (r0 >= len) continue;
+    const int nv = (int)(len - r0 < kRowsPerCta ? len - r0 : kRowsPerCta) * nvec;
+    for (int base = 0; base < nv; base += kCopyThreads * kUnroll) {
+      T val[kUnroll];
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        const int i = base + u * kCopyThreads + threadIdx.x;
+        val[u] = T{};
+        if (i < nv && src) {
+          const int t = i / nvec, v = i - t * nvec;
+          val[u] = *reinterpret_cast<const T*>(src + (r0 + t) * sr + (long long)v * V);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        const int i = base + u * kCopyThreads + threadIdx.x;
+        if (i < nv) {
+          const int t = i / nvec, v = i - t * nvec;
+          *reinterpret_cast<T*>(out + (dst0 + r0 + t) * row_bytes + (long long)v * V) = val[u];
+        }
+      }
+    }
   }
 }
 
 // out[b][h][n] = packed[h][cu[b] + n] for n < len(b), zero otherwise.
 template <int V>
-__global__ void unpack_rows_kernel(const uint8_t* __restrict__ packed, long long total_tokens, int H, int row_bytes,
-                                   const int* __restrict__ cu, int B, int N, uint8_t* __restrict__ out) {
+__global__ void __launch_bounds__(kCopyThreads) unpack_rows_kernel(const uint8_t* __restrict__ packed,
+                                                                   long long total_tokens, int H, int row_bytes,
+                                                                   const int* __restrict__ cu, int B, int N,
+                                                                   uint8_t* __restrict__ out) {
   using T = typename VecT<V>::T;
   const int nvec = row_bytes / V;
-  const long long n = (long long)B * H * N * nvec;
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
-    const long long row = i / nvec;
-    const int v = (int)(i - row * nvec);
-    const int t = (int)(row % N);
-    const long long bh = row / N;
-    const int h = (int)(bh % H);
-    const int b = (int)(bh / H);
-    const int s = cu[b];
-    T val{};
-    if (t < cu[b + 1] - s)
-      val = *reinterpret_cast<const T*>(packed + ((long long)h * total_tokens + s + t) * row_bytes + (long long)v * V);
-    *reinterpret_cast<T*>(out + row * row_bytes + (long long)v * V) = val;
+  const int h = blockIdx.y;
+  const int r0 = blockIdx.x * kRowsPerCta;
+  const int nv = min(kRowsPerCta, N - r0) * nvec;
+  for (int b = blockIdx.z; b < B; b += gridDim.z) {
+    const int s0 = __ldg(cu + b);
+    const int len = __ldg(cu + b + 1) - s0;
+    const uint8_t* src = packed + ((long long)h * total_tokens + s0) * row_bytes;
+    uint8_t* dst = out + (((long long)b * H + h) * N + r0) * row_bytes;
+    for (int base = 0; base < nv; base += kCopyThreads * kUnroll) {
+      T val[kUnroll];
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        const int i = base + u * kCopyThreads + threadIdx.x;
+        val[u] = T{};
+        const int t = i / nvec;
+        if (i < nv && r0 + t < len) val[u] = *reinterpret_cast<const T*>(src + (long long)(r0 + t) * row_bytes + (long long)(i - t * nvec) * V);
+      }
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        const int i = base + u * kCopyThreads + threadIdx.x;
+        if (i < nv) *reinterpret_cast<T*>(dst + (long long)i * V) = val[u];
+      }
+    }
   }
 }
 
@@ -224,13 +261,16 @@ extern "C" int fmlm_pack_rows(const fmlm_view4* x, int32_t elem_bytes, int32_t h
                       (long long)reinterpret_cast<uintptr_t>(out)})
     g = std::__gcd(g, a == 0 ? g : a);
   const int V = pick_vec(g);
-  const long long n = n_rows * (row_bytes / V);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   auto px = reinterpret_cast<const uint8_t*>(x->data);
   auto po = reinterpret_cast<uint8_t*>(out);
-#define FMLM_PACK(VV)                                                                                            \
-  pack_rows_kernel<VV><<<grid_for(n), 256, 0, s>>>(px, sb, sh, sr, (int)row_bytes, H, cu_seqlens, B, total_tokens, \
-                                                   total_padded, po)
+  const long long max_rows = std::max<long long>(x->rows, total_padded - total_tokens);
+  const dim3 pgrid((unsigned)((max_rows + kRowsPerCta - 1) / kRowsPerCta), (unsigned)H,
+                   (unsigned)std::min<long long>((long long)B + 1, 65535));
+  if (H > 65535 || pgrid.x == 0) return set_error(FMLM_ERR_INVALID, "bad pack sizes");
+#define FMLM_PACK(VV) \
+  pack_rows_kernel<VV><<<pgrid, kCopyThreads, 0, s>>>(px, sb, sh, sr, (int)row_bytes, cu_seqlens, B, total_tokens, \
+                                                      total_padded, po)
   switch (V) {
     case 16: FMLM_PACK(16); break;
     case 8: FMLM_PACK(8); break;
@@ -255,12 +295,13 @@ extern "C" int fmlm_unpack_rows(const void* packed, int64_t total_tokens, int32_
   for (long long a : {(long long)reinterpret_cast<uintptr_t>(packed), (long long)reinterpret_cast<uintptr_t>(out)})
     g = std::__gcd(g, a == 0 ? g : a);
   const int V = pick_vec(g);
-  const long long n = n_rows * (row_bytes / V);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   auto pp = reinterpret_cast<const uint8_t*>(packed);
   auto po = reinterpret_cast<uint8_t*>(out);
+  const dim3 ugrid((unsigned)((N + kRowsPerCta - 1) / kRowsPerCta), (unsigned)H, (unsigned)std::min(B, 65535));
+  if (H > 65535) return set_error(FMLM_ERR_INVALID, "bad unpack sizes");
 #define FMLM_UNPACK(VV) \
-  unpack_rows_kernel<VV><<<grid_for(n), 256, 0, s>>>(pp, total_tokens, H, (int)row_bytes, cu_seqlens, B, N, po)
+  unpack_rows_kernel<VV><<<ugrid, kCopyThreads, 0, s>>>(pp, total_tokens, H, (int)row_bytes, cu_seqlens, B, N, po)
   switch (V) {
     case 16: FMLM_UNPACK(16); break;
     case 8: FMLM_UNPACK(8); break;

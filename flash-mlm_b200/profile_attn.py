@@ -10,6 +10,9 @@ D=64 bf16 + shared 1024 context; 4 MLA B=16 H=128 D=512 + 4096 context per
 sequence; 3 packed causal B=64 H=12 N=256 D=64 f16 +
 per-sequence context U[256,2048]; 5a packed B=8 H=16 N=512 D=128 bf16 +
 per-sequence context --ctx; 5b packed B=--batch H=16 N=512 D=128 bf16, no context.
+`--op pack` / `--op unpack` run the packing kernels on config 2's shapes
+instead (pack_and_pad_main_tensors_for_mlm_compressed of q/k/v, and
+unpack_from_kernel of a packed [H*T, D] output).
 Equivalent of the reference's src/profile/profile_mlm_ncu.py.
 """
 
@@ -90,8 +93,25 @@ def build(config: str, ctx: int, batch: int, device):
                                                        causal_query_seq_attn=causal)
 
 
+def build_pack_op(op: str, device):
+    """Config 2 shapes (B=32, H=16, N=512, D=64, bf16, lengths U[64,512])."""
+    from flash_mlm.host import host_utils
+
+    g = torch.Generator().manual_seed(0)
+    B, H, N, D = 32, 16, 512, 64
+    lengths = _lengths(g, B, 64, 512)
+    meta = flash_mlm.build_pack_metadata(lengths.to(device), N, 64)
+    if op == "pack":
+        q, k, v = (torch.randn((B, H, N, D), generator=g).to(torch.bfloat16).to(device) for _ in range(3))
+        return lambda: host_utils.pack_and_pad_main_tensors_for_mlm_compressed(q, k, v, q_meta=meta, num_heads=H,
+                                                                              is_mla=False, block_m=64, block_n=64)
+    packed = torch.randn((H * meta.total_tokens, D), generator=g).to(torch.bfloat16).to(device)
+    return lambda: flash_mlm.unpack_from_kernel(packed, meta, H)
+
+
 def main():
     ap = argparse.ArgumentParser()
+    ap.add_argument("--op", default="attn", choices=["attn", "pack", "unpack"])
     ap.add_argument("--config", default="2")
     ap.add_argument("--ctx", type=int, default=4096)
     ap.add_argument("--batch", type=int, default=32)
@@ -99,7 +119,7 @@ def main():
     ap.add_argument("--iters", type=int, default=1)
     args = ap.parse_args()
     device = torch.device("cuda", 0)
-    step = build(args.config, args.ctx, args.batch, device)
+    step = build(args.config, args.ctx, args.batch, device) if args.op == "attn" else build_pack_op(args.op, device)
     for _ in range(args.warmup + args.iters):
         step()
     torch.cuda.synchronize()
