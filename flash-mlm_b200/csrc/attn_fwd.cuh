@@ -57,6 +57,8 @@ struct AttnParams {
   int* work;        // packed: schedule workspace (layout at kWorkHeader)
   void* out;        // [rows, D]
   int* err;         // device error word
+  const uint16_t* q_ptr;          // TQ: q itself (16-bit elements), read by the softmax warps
+  long long q_sb, q_sh, q_sr;     // its batch / head / row strides in elements
   unsigned long long timeout_ns;
   unsigned long long* trace;  // optional timeline buffer (builds with FMLM_TRACE only)
 };
@@ -103,12 +105,22 @@ struct AttnCfg {
 #ifndef FMLM_BN_D128
 #define FMLM_BN_D128 128
 #endif
-  static constexpr int BN = (D == 512) ? 32 : (D >= 256) ? 64 : (D == 128) ? FMLM_BN_D128 : 128;  // key rows per block
+#ifndef FMLM_MLA_TQ
+#define FMLM_MLA_TQ 1
+#endif
+  // D = 512: Q columns [QS, D) are kept in TMEM instead of shared memory and
+  // that half of S = Q Kᵀ is issued with A from TMEM.  The 64 KB this frees
+  // holds 64-key K tiles (S at N=64) instead of 32-key ones (N=32, a third of
+  // the tensor rate).
+  static constexpr bool TQ = FMLM_MLA_TQ && D == 512;
+  static constexpr int QS = TQ ? D / 2 : D;        // Q columns staged in shared memory
+  static constexpr int BN = (D == 512) ? (TQ ? 64 : 32) : (D >= 256) ? 64 : (D == 128) ? FMLM_BN_D128 : 128;  // key rows per block
   static constexpr int PAIR = NQ * BM;             // query rows per work item
   static constexpr int SWB = (D * 2 >= 128) ? 128 : D * 2;  // swizzle span in bytes
   static constexpr int SLAB_COLS = SWB / 2;
   static constexpr int NSLAB = D / SLAB_COLS;
-  static constexpr int Q_BYTES = BM * D * 2;
+  static constexpr int Q_BYTES = BM * QS * 2;
+  static constexpr int Q_NSLAB = QS / SLAB_COLS;
   static constexpr int KV_BYTES = BN * D * 2;
   // One tile per CTA at D <= 64 runs two CTAs per SM (TMEM 256 columns and
   // about 80 KB of shared memory each): the two CTAs work on independent items.
@@ -125,7 +137,7 @@ struct AttnCfg {
   // Q buffers: with two, the next item's Q is loaded while the current item
   // still computes, so its first S is ready when the softmax reaches it.
   static constexpr int QBUF = (CTAS_PER_SM == 2) ? FMLM_QBUF_2CTA : 1;
-  static constexpr int STAGES = (CTAS_PER_SM == 2) ? (QBUF == 2 ? 2 : FMLM_STAGES_2CTA) : (D <= 32) ? 4 : (D <= 64) ? 3 : (D == 512) ? 3
+  static constexpr int STAGES = (CTAS_PER_SM == 2) ? (QBUF == 2 ? 2 : FMLM_STAGES_2CTA) : (D <= 32) ? 4 : (D <= 64) ? 3 : (D == 512) ? (TQ ? 2 : 3)
                               : (D == 128 && BN == 64) ? 4 : 2;
   static constexpr int NUM_SOFTMAX_WARPS = 4 * NQ;
   static constexpr int TMA_WARP = NUM_SOFTMAX_WARPS;
@@ -142,11 +154,18 @@ struct AttnCfg {
   // P gets its own TMEM columns when they fit (D <= 64 with two tiles, or one
   // tile): S_t(j+1) can then be issued as soon as the softmax has read S_t(j).
   // Otherwise P is written over the first BN/2 columns of S_t.
-  static constexpr bool SEP_P = NQ * (BN + DV + BN / 2) <= 512;
-  static constexpr int TM_S = 0;                   // S_t at column t*BN
-  static constexpr int TM_O = NQ * BN;             // O_t at column TM_O + t*DV
+  // SDB (with TQ): two S buffers, P written over the first half of its own
+  // S buffer, so S(j+1) is queued on the tensor pipe while the softmax works
+  // on S(j); a buffer is reused only after the PV that read its P was issued
+  // (tcgen05 ops of one thread run in order).
+  static constexpr bool SDB = TQ;
+  static constexpr bool SEP_P = !SDB && NQ * (BN + DV + BN / 2) <= 512;
+  static constexpr int TM_S = 0;                   // S_t at column t*BN (SDB: buffer b at b*BN)
+  static constexpr int TM_O = SDB ? 2 * BN : NQ * BN;  // O_t at column TM_O + t*DV
   static constexpr int TM_P = SEP_P ? NQ * (BN + DV) : 0;  // P_t at TM_P + t*BN/2 (or over S_t)
-  static constexpr int TMEM_USED = NQ * (BN + DV) + (SEP_P ? NQ * BN / 2 : 0);
+  static constexpr int TM_Q1 = 384;                // TQ: Q columns [QS, D) as packed pairs, (D - QS) / 2 columns
+  static constexpr int TMEM_USED = TQ ? TM_Q1 + (D - QS) / 2 : NQ * (BN + DV) + (SEP_P ? NQ * BN / 2 : 0);
+  static_assert(!TQ || (NQ == 1 && SDB && 2 * BN + DV <= TM_Q1), "TQ TMEM layout");
   static constexpr int TMEM_COLS = TMEM_USED <= 32 ? 32 : TMEM_USED <= 64 ? 64 : TMEM_USED <= 128 ? 128
                                  : TMEM_USED <= 256 ? 256 : 512;
   static_assert(TMEM_USED <= 512, "TMEM budget");
@@ -263,6 +282,7 @@ struct __align__(8) AttnBarriers {
   uint64_t item_full[4], item_empty[4];  // ring of work-item indices, producer -> other roles
   int item_idx[4];
   uint64_t exp_tok[2];  // two-tile ping-pong: tile t may run its exp2 loop
+  uint64_t q1_full;     // TQ: the softmax warps have written this item's Q columns [QS, D) to TMEM
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -344,6 +364,7 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
       mbar_init(&bar->item_full[i], 1);
       mbar_init(&bar->item_empty[i], 5 * NQ);  // every MMA and softmax warp
     }
+    mbar_init(&bar->q1_full, 4);
     mbar_init(&bar->exp_tok[0], 4);
     mbar_init(&bar->exp_tok[1], 4);
     bar->abort_flag = 0;
@@ -433,7 +454,7 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
 #pragma unroll
         for (int t = 0; t < NQ; ++t) {
           if (q_it.qrows(t) == 0) continue;
-          for (int s = 0; s < C::NSLAB; ++s)
+          for (int s = 0; s < C::Q_NSLAB; ++s)
             tma_load_4d(sQ + (qs * NQ + t) * C::Q_BYTES + s * (BM * SWB), &tm_q, &bar->q_full[qs], s * C::SLAB_COLS,
                         q_it.qrow0 + t * BM, q_it.qh, q_it.qb);
         }
@@ -550,29 +571,34 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
     const uint32_t tO_d = tmem_base + C::TM_O + t * C::DV;
     const uint32_t tP_a = tmem_base + (C::SEP_P ? C::TM_P + t * (BN / 2) : C::TM_S + t * BN);
     const bool leader = elect_one();
-    uint32_t p_ph = 0, o_empty_ph = 1, s_free_ph = 0;
+    uint32_t p_ph = 0, o_empty_ph = 1, s_free_ph = 0, q1_ph = 0;
+    uint32_t gb = 0;  // SDB: key blocks issued so far (S buffer gb & 1, its (gb >> 1)-th use)
     bool first_item = true;
     uint32_t fill = 0;
 
-    auto issue_s = [&](int st) {
+    auto issue_s = [&](int st, uint32_t d_col = 0) {
       if (leader) {
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t slab = (kk * 32) / SWB, inrow = (kk * 32) % SWB;
-          const uint64_t a = make_smem_desc(sQa + slab * (BM * SWB) + inrow, 16, 8 * SWB, layout);
           const uint64_t b = make_smem_desc(sKa + st * C::KV_BYTES + slab * (BN * SWB) + inrow, 16, 8 * SWB, layout);
-          umma_ss(tS_d, a, b, idesc_qk, kk > 0 ? 1u : 0u);
+          if (C::TQ && kk >= C::QS / 16) {
+            umma_ts(tS_d + d_col, tmem_base + C::TM_Q1 + (kk - C::QS / 16) * 8, b, idesc_qk, 1u);
+          } else {
+            const uint64_t a = make_smem_desc(sQa + slab * (BM * SWB) + inrow, 16, 8 * SWB, layout);
+            umma_ss(tS_d + d_col, a, b, idesc_qk, kk > 0 ? 1u : 0u);
+          }
         }
       }
     };
-    auto issue_pv = [&](int st, bool acc, int dh) {
+    auto issue_pv = [&](int st, bool acc, int dh, uint32_t p_col = 0) {
       if (leader) {
         // V columns [dh*DV, dh*DV + DV) start at slab dh*DV/SLAB_COLS of the tile.
         const uint32_t vbase = (mla ? sKa : sVa) + st * C::KV_BYTES + (dh * C::DV / C::SLAB_COLS) * (BN * SWB);
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk) {
           const uint64_t b = make_smem_desc(vbase + kk * 16 * SWB, BN * SWB, 8 * SWB, layout);
-          umma_ts(tO_d, tP_a + kk * 8, b, idesc_pv, (acc || kk > 0) ? 1u : 0u);
+          umma_ts(tO_d, tP_a + p_col + kk * 8, b, idesc_pv, (acc || kk > 0) ? 1u : 0u);
         }
       }
     };
@@ -607,6 +633,46 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
         fill += nb;
         continue;
       }
+      if constexpr (C::SDB) {
+        // Order on the tensor pipe: S(0), S(1), PV(0), S(2), PV(1), ...
+        // S(g+1) overwrites buffer (g+1) & 1, whose P(g-1) was read by PV(g-1),
+        // issued in the previous iteration.  MLA only: V is the K tile.
+        bool ok = true;
+        for (int j = -1; j < nb && ok; ++j) {
+          if (j + 1 < nb) {
+            const uint32_t g1 = gb + j + 1;
+            const int st1 = (fill + j + 1) % STAGES;
+            if (!wait(&bar->k_full[st1], ((fill + j + 1) / STAGES) & 1u)) { ok = false; break; }
+            if (j < 0) {
+              // the softmax warps' copy of this item's Q columns [QS, D) into TMEM
+              if (!wait(&bar->q1_full, q1_ph)) { ok = false; break; }
+              q1_ph ^= 1u;
+            }
+            tc_fence_after();
+            issue_s(st1, (g1 & 1u) * BN);
+            commit(&bar->s_full[g1 & 1u]);
+            FMLM_TR(32);
+            if (j + 2 == nb) commit(q_empty);
+          }
+          if (j < 0) continue;
+          const uint32_t g = gb + j, b = g & 1u;
+          const int st = (fill + j) % STAGES;
+          if (!wait(&bar->p_full[b], (g >> 1) & 1u)) { ok = false; break; }
+          FMLM_TR(30);
+          if (j == 0) {
+            if (!wait(&bar->o_empty[0], o_empty_ph)) { ok = false; break; }
+            o_empty_ph ^= 1u;
+          }
+          tc_fence_after();
+          issue_pv(st, j > 0, it.dh, b * BN);
+          commit(&bar->pv_done[0]);
+          commit(&bar->kv_empty[st]);
+        }
+        if (!ok) break;
+        gb += nb;
+        fill += nb;
+        continue;
+      }
       {
         const int st = fill % STAGES;
         if (!wait(&bar->k_full[st], (fill / STAGES) & 1u)) break;
@@ -616,6 +682,11 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
           s_free_ph ^= 1u;
         }
         first_item = false;
+        if constexpr (C::TQ) {
+          // the softmax warps' copy of this item's Q columns [QS, D) into TMEM
+          if (!wait(&bar->q1_full, q1_ph)) break;
+          q1_ph ^= 1u;
+        }
         tc_fence_after();
         issue_s(st);
         commit(&bar->s_full[t]);
@@ -690,6 +761,7 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
     const bool pos_scale = sl2 > 0.f;
     const float fac = pos_scale ? sl2 : 1.0f;
     uint32_t s_ph = 0, o_ph = 0, pv_ph = 0, tok_ph = 0;
+    uint32_t gblk = 0;  // SDB: key blocks processed so far (same count as the MMA warp's)
     T* out = reinterpret_cast<T*>(p.out);
     // With two tiles the exp2 loops of the tiles alternate (a token passed
     // through exp_tok), so one tile's MUFU-bound loop overlaps the other's
@@ -708,22 +780,46 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
       const bool pp = kPingPong && it.qrows0 > 0 && it.qrows1 > 0;
       float m = -INFINITY, l = 0.f;
       const int nb = it.nblocks();
+      if constexpr (C::TQ) {
+        // Q columns [QS, D) of this thread's row go to TMEM lane `row` as
+        // packed pairs (the layout of a TMEM A operand).  Every MMA of the
+        // previous item has completed (its epilogue waited for the last PV).
+        constexpr int NW = (D - C::QS) / 2;  // 32-bit words per row
+        const uint16_t* qrow = p.q_ptr + (long long)it.qb * p.q_sb + (long long)it.qh * p.q_sh +
+                               (long long)(it.qrow0 + row) * p.q_sr + C::QS;
+        const uint32_t tQ1 = tmem_base + lane_off + C::TM_Q1;
+#pragma unroll
+        for (int c0 = 0; c0 < NW; c0 += 64) {
+          uint32_t qv[64];
+#pragma unroll
+          for (int q = 0; q < 16; ++q) {
+            const uint4 u = row_valid ? __ldg(reinterpret_cast<const uint4*>(qrow) + c0 / 4 + q) : make_uint4(0, 0, 0, 0);
+            qv[4 * q] = u.x; qv[4 * q + 1] = u.y; qv[4 * q + 2] = u.z; qv[4 * q + 3] = u.w;
+          }
+          tmem_st_x64(tQ1 + c0, qv);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bar->q1_full);
+      }
       {
         for (int j = 0; j < nb; ++j) {
           int brow;
           const Seg sgm = it.block_seg(j, BN, brow);
           int kvv = min(BN, sgm.row1 - brow);
           if (!row_valid) kvv = 0;
-          if (!mbar_wait(&bar->s_full[t], s_ph, abort_flag, tmo)) { fail(); }
+          const uint32_t g = gblk + j, sb = C::SDB ? (g & 1u) : 0u;
+          const uint32_t tSb = tS + sb * BN, tPb = tP + sb * BN;  // SDB: S buffer g & 1, P over it
+          if (!mbar_wait(&bar->s_full[C::SDB ? sb : t], C::SDB ? ((g >> 1) & 1u) : s_ph, abort_flag, tmo)) { fail(); }
           failed = __any_sync(0xffffffffu, failed);
           if (failed) break;
           FMLM_TR(10 + t);
           s_ph ^= 1u;
           tc_fence_after();
           uint32_t r[BN];
-          if constexpr (BN == 128) tmem_ld_x128(tS, r);
-          else if constexpr (BN == 64) tmem_ld_x64(tS, r);
-          else tmem_ld_x32(tS, r);
+          if constexpr (BN == 128) tmem_ld_x128(tSb, r);
+          else if constexpr (BN == 64) tmem_ld_x64(tSb, r);
+          else tmem_ld_x32(tSb, r);
           FMLM_TR(12 + t);
           if constexpr (C::SEP_P) {
             // S_t is in registers: the MMA warp may overwrite it with S_t(j+1).
@@ -811,8 +907,8 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
                 pk[cc] = *reinterpret_cast<uint32_t*>(&v2);
               }
             }
-            if constexpr (PC == 32) tmem_st_x32_nowait(tP + h0, pk);
-            else tmem_st_x16_nowait(tP + h0, pk);
+            if constexpr (PC == 32) tmem_st_x32_nowait(tPb + h0, pk);
+            else tmem_st_x16_nowait(tPb + h0, pk);
           }
           if (pp) {
             __syncwarp();
@@ -822,7 +918,15 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
           FMLM_TR(14 + t);
           if (__any_sync(0xffffffffu, need)) {
             // O holds PV(0..j-1), all complete (aliased P: PV_t(j-1) was issued
-            // before S_t(j); separate P: waited above); PV_t(j) waits for p_full.
+            // before S_t(j); separate P: waited above; SDB: S(j) was issued
+            // before PV(j-1), so PV(j-1) is waited for here); PV_t(j) waits
+            // for p_full.
+            if constexpr (C::SDB) {
+              if (!mbar_wait(&bar->pv_done[0], (g - 1) & 1u, abort_flag, tmo)) fail();
+              failed = __any_sync(0xffffffffu, failed);
+              if (failed) break;
+              tc_fence_after();
+            }
 #pragma unroll
             for (int c0 = 0; c0 < C::DV; c0 += OC) {
               uint32_t o[OC];
@@ -835,14 +939,18 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
           tmem_wait_st();
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(&bar->p_full[t]);
+          if (lane == 0) mbar_arrive(&bar->p_full[C::SDB ? sb : t]);
           FMLM_TR(16 + t);
         }
         if (failed) break;
       }
       if (failed) break;
       // epilogue: O / l  ->  global
-      if constexpr (C::SEP_P) {
+      if constexpr (C::SDB) {
+        const uint32_t gl = gblk + nb - 1;
+        gblk += nb;
+        if (!mbar_wait(&bar->pv_done[0], gl & 1u, abort_flag, tmo)) fail();
+      } else if constexpr (C::SEP_P) {
         if (!mbar_wait(&bar->pv_done[t], pv_ph, abort_flag, tmo)) fail();
         pv_ph ^= 1u;
       } else {

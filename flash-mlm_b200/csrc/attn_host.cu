@@ -295,6 +295,10 @@ extern "C" int fmlm_attn_dense_fwd(const fmlm_dense_args* a, void* stream) {
   p.out = a->out;
   if (!a->error_word) return set_error(FMLM_ERR_INVALID, "error_word is required");
   p.err = a->error_word;
+  p.q_ptr = reinterpret_cast<const uint16_t*>(a->q.data);
+  p.q_sb = a->q.batch_stride;
+  p.q_sh = a->q.head_stride;
+  p.q_sr = a->q.row_stride;
   p.timeout_ns = kTimeoutNs;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   return a->dtype == FMLM_DTYPE_BF16 ? dispatch<true>(D, m, p, items, s) : dispatch<false>(D, m, p, items, s);
@@ -368,6 +372,10 @@ extern "C" int fmlm_attn_packed_fwd(const fmlm_packed_args* a, void* stream) {
   p.work = work;
   p.out = a->out;
   p.err = a->error_word;
+  p.q_ptr = reinterpret_cast<const uint16_t*>(a->q.data);
+  p.q_sb = a->q.batch_stride;
+  p.q_sh = a->q.head_stride;
+  p.q_sr = a->q.row_stride;
   p.timeout_ns = kTimeoutNs;
 #ifdef FMLM_TRACE
   p.trace = g_trace_buffer;
