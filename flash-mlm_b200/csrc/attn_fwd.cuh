@@ -114,7 +114,10 @@ struct AttnCfg {
   // the tensor rate).
   static constexpr bool TQ = FMLM_MLA_TQ && D == 512;
   static constexpr int QS = TQ ? D / 2 : D;        // Q columns staged in shared memory
-  static constexpr int BN = (D == 512) ? (TQ ? 64 : 32) : (D >= 256) ? 64 : (D == 128) ? FMLM_BN_D128 : 128;  // key rows per block
+#ifndef FMLM_MLA_BN
+#define FMLM_MLA_BN 48
+#endif
+  static constexpr int BN = (D == 512) ? (TQ ? FMLM_MLA_BN : 32) : (D >= 256) ? 64 : (D == 128) ? FMLM_BN_D128 : 128;  // key rows per block
   static constexpr int PAIR = NQ * BM;             // query rows per work item
   static constexpr int SWB = (D * 2 >= 128) ? 128 : D * 2;  // swizzle span in bytes
   static constexpr int SLAB_COLS = SWB / 2;
@@ -137,7 +140,7 @@ struct AttnCfg {
   // Q buffers: with two, the next item's Q is loaded while the current item
   // still computes, so its first S is ready when the softmax reaches it.
   static constexpr int QBUF = (CTAS_PER_SM == 2) ? FMLM_QBUF_2CTA : 1;
-  static constexpr int STAGES = (CTAS_PER_SM == 2) ? (QBUF == 2 ? 2 : FMLM_STAGES_2CTA) : (D <= 32) ? 4 : (D <= 64) ? 3 : (D == 512) ? (TQ ? 2 : 3)
+  static constexpr int STAGES = (CTAS_PER_SM == 2) ? (QBUF == 2 ? 2 : FMLM_STAGES_2CTA) : (D <= 32) ? 4 : (D <= 64) ? 3 : (D == 512) ? (TQ ? (BN <= 48 ? 3 : 2) : 3)
                               : (D == 128 && BN == 64) ? 4 : 2;
   static constexpr int NUM_SOFTMAX_WARPS = 4 * NQ;
   static constexpr int TMA_WARP = NUM_SOFTMAX_WARPS;
@@ -819,6 +822,7 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
           uint32_t r[BN];
           if constexpr (BN == 128) tmem_ld_x128(tSb, r);
           else if constexpr (BN == 64) tmem_ld_x64(tSb, r);
+          else if constexpr (BN == 48) tmem_ld_x48(tSb, r);
           else tmem_ld_x32(tSb, r);
           FMLM_TR(12 + t);
           if constexpr (C::SEP_P) {
@@ -908,6 +912,7 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
               }
             }
             if constexpr (PC == 32) tmem_st_x32_nowait(tPb + h0, pk);
+            else if constexpr (PC == 24) tmem_st_x24_nowait(tPb + h0, pk);
             else tmem_st_x16_nowait(tPb + h0, pk);
           }
           if (pp) {
