@@ -44,6 +44,34 @@ class PackingCache:
     def __init__(self):
         self._buffers: dict[tuple, torch.Tensor] = {}
         self._pack_meta: dict[tuple, PackMetadata] = {}
+        # Device tile schedules of recent packed launches (see schedule_workspace).
+        self._schedules: list[tuple[tuple, tuple, torch.Tensor]] = []
+
+    _MAX_SCHEDULES = 8
+
+    def schedule_workspace(self, tensors: tuple, scalars: tuple, nbytes: int,
+                           device: torch.device) -> tuple[torch.Tensor, bool]:
+        """Workspace for a packed launch's device tile schedule, and whether it already holds it.
+
+        The schedule is a function of the sequence-offset tensors (``tensors``:
+        cu_seqlens_q and, with a context, cu_seqlens_kv) and of ``scalars``.  An
+        entry matches only the same tensor objects at the same in-place version
+        (``Tensor._version``), so a new or modified offsets tensor builds a new
+        schedule; entries keep their tensors alive, so an address cannot be
+        reused by another tensor while an entry refers to it.  At most
+        ``_MAX_SCHEDULES`` entries are kept (least recently used dropped).
+        """
+        versions = tuple(t._version for t in tensors)
+        for i, (ts, key, ws) in enumerate(self._schedules):
+            if (key == (scalars, versions) and len(ts) == len(tensors)
+                    and all(a is b for a, b in zip(ts, tensors)) and ws.numel() * 4 >= nbytes):
+                self._schedules.append(self._schedules.pop(i))
+                return ws, True
+        ws = torch.empty(((nbytes + 15) // 16, 4), dtype=torch.int32, device=device)
+        self._schedules.append((tuple(tensors), (scalars, versions), ws))
+        if len(self._schedules) > self._MAX_SCHEDULES:
+            self._schedules.pop(0)
+        return ws, False
 
     def get_2d(self, name: str, rows: int, cols: int, *, dtype: torch.dtype, device: torch.device) -> torch.Tensor:
         if rows < 0:
@@ -71,6 +99,7 @@ class PackingCache:
     def clear(self):
         self._buffers.clear()
         self._pack_meta.clear()
+        self._schedules.clear()
 
 
 @dataclass

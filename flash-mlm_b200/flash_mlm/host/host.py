@@ -177,7 +177,16 @@ def _packed_launch(*, q_view, k_view, v_view, q_layout, kv_layout, seq_len, tota
     args.out_rows_per_head = out_rows_per_head
     L = _lib.lib()
     nbytes = L.fmlm_packed_workspace_bytes(batch, total_q_len, d)
-    ws = _workspace(device, nbytes, cache)
+    if cache is not None:
+        # A repeated call with the same offsets tensors reuses its device tile
+        # schedule instead of rebuilding it.
+        key_tensors = (cu_seqlens_q, ctx.cu_seqlens_kv) if has_ctx else (cu_seqlens_q,)
+        key_scalars = (device.type, device.index, d, batch, total_q_len, int(has_ctx), int(causal),
+                       int(ctx.context_batch_size) if has_ctx else 0)
+        ws, cached = cache.packing.schedule_workspace(key_tensors, key_scalars, nbytes, device)
+        args.reuse_schedule = int(cached)
+    else:
+        ws = _workspace(device, nbytes, None)
     args.workspace = ws.data_ptr()
     args.workspace_bytes = ws.numel() * 4
     args.error_word = _lib.error_word(device).data_ptr()

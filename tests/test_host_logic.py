@@ -187,3 +187,31 @@ def test_c_abi_rejects_bad_arguments_without_a_gpu():
     assert L.fmlm_attn_packed_fwd(ctypes.byref(a), None) == -2
     assert "HEAD_DIM" in L.fmlm_last_error().decode()
     assert L.fmlm_build_pack_metadata(None, 2, 4, 0, None, None, None, None, None, None) == -1
+
+
+def test_schedule_workspace_memo_rules():
+    """A schedule is reused only for the same offsets tensors at the same version and scalars."""
+    from flash_mlm.host.cache import PackingCache
+
+    pc = PackingCache()
+    dev = torch.device("cpu")
+    cu = torch.tensor([0, 5, 9], dtype=torch.int32)
+    ws1, hit1 = pc.schedule_workspace((cu,), ("k", 1), 64, dev)
+    ws2, hit2 = pc.schedule_workspace((cu,), ("k", 1), 64, dev)
+    assert not hit1 and hit2 and ws2 is ws1
+    # different scalars, an equal-valued but different tensor, or an in-place change: rebuild
+    assert not pc.schedule_workspace((cu,), ("k", 2), 64, dev)[1]
+    assert not pc.schedule_workspace((cu.clone(),), ("k", 1), 64, dev)[1]
+    cu.add_(0)
+    assert not pc.schedule_workspace((cu,), ("k", 1), 64, dev)[1]
+    assert pc.schedule_workspace((cu,), ("k", 1), 64, dev)[1]
+    # a larger workspace requirement does not reuse a smaller buffer
+    assert not pc.schedule_workspace((cu,), ("k", 1), 4096, dev)[1]
+    # bounded, least recently used dropped
+    keep = [torch.zeros(2, dtype=torch.int32) for _ in range(PackingCache._MAX_SCHEDULES + 2)]
+    for t in keep:
+        pc.schedule_workspace((t,), ("k",), 64, dev)
+    assert len(pc._schedules) == PackingCache._MAX_SCHEDULES
+    assert not pc.schedule_workspace((keep[0],), ("k",), 64, dev)[1]
+    pc.clear()
+    assert pc._schedules == []
