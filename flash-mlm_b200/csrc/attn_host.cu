@@ -213,13 +213,17 @@ int launch_attn(const CUtensorMap* m, const AttnParams& p, long long items, cuda
   return check_launch("attn_fwd_kernel");
 }
 
+// single_tile (head_dim 128 only): one 128-row query tile per work item, for
+// problems with fewer tile pairs than SMs (twice the items; P gets its own
+// TMEM columns, so S(j+1) does not wait for PV(j)).
 template <bool BF16>
-int dispatch(int D, const CUtensorMap* m, const AttnParams& p, long long items, cudaStream_t s) {
+int dispatch(int D, const CUtensorMap* m, const AttnParams& p, long long items, cudaStream_t s,
+             bool single_tile = false) {
   switch (D) {
     case 16: return launch_attn<16, 2, BF16>(m, p, items, s);
     case 32: return launch_attn<32, 2, BF16>(m, p, items, s);
     case 64: return launch_attn<64, FMLM_NQ_D64, BF16>(m, p, items, s);
-    case 128: return launch_attn<128, 2, BF16>(m, p, items, s);
+    case 128: return single_tile ? launch_attn<128, 1, BF16>(m, p, items, s) : launch_attn<128, 2, BF16>(m, p, items, s);
     case 256: return launch_attn<256, 1, BF16>(m, p, items, s);
     case 512: return launch_attn<512, 1, BF16>(m, p, items, s);
     default: return set_error(FMLM_ERR_UNSUPPORTED, "head_dim %d is not supported", D);
@@ -304,8 +308,15 @@ extern "C" int fmlm_attn_dense_fwd(const fmlm_dense_args* a, void* stream) {
   return a->dtype == FMLM_DTYPE_BF16 ? dispatch<true>(D, m, p, items, s) : dispatch<false>(D, m, p, items, s);
 }
 
+// Packed launches at head_dim 128 use single-tile items when the problem has
+// fewer tile pairs than the GPU has SMs.
+bool packed_single_tile(int D, int64_t total_q_len, int batch, int heads) {
+  return D == 128 && (total_q_len / pair_rows(D) + batch) * (int64_t)heads < device_sm_count();
+}
+
 extern "C" size_t fmlm_packed_workspace_bytes(int32_t batch, int64_t total_q_len, int32_t head_dim) {
-  const int64_t pr = head_dim > 0 ? pair_rows(head_dim) : 128;
+  // sized for the finer of the two item granularities head_dim 128 may use
+  const int64_t pr = head_dim > 0 ? (head_dim == 128 ? 128 : pair_rows(head_dim)) : 128;
   const int64_t cap = total_q_len / pr + batch + 2;
   return (size_t)((cap + kWorkHeader) * sizeof(int32_t) + 15) / 16 * 16;
 }
@@ -345,7 +356,8 @@ extern "C" int fmlm_attn_packed_fwd(const fmlm_packed_args* a, void* stream) {
                         "v_cache")))
     return rc;
 
-  const int pr = pair_rows(D);
+  const bool single = packed_single_tile(D, a->total_q_len, a->batch, a->num_heads);
+  const int pr = single ? 128 : pair_rows(D);
   const int64_t cap = a->total_q_len / pr + a->batch + 2;
   int* work = reinterpret_cast<int*>(a->workspace);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
@@ -381,8 +393,8 @@ extern "C" int fmlm_attn_packed_fwd(const fmlm_packed_args* a, void* stream) {
   p.trace = g_trace_buffer;
 #endif
   const long long items_bound = cap * (long long)a->num_heads * o_halves(D);
-  return a->dtype == FMLM_DTYPE_BF16 ? dispatch<true>(D, m, p, items_bound, s)
-                                     : dispatch<false>(D, m, p, items_bound, s);
+  return a->dtype == FMLM_DTYPE_BF16 ? dispatch<true>(D, m, p, items_bound, s, single)
+                                     : dispatch<false>(D, m, p, items_bound, s, single);
 }
 
 #ifdef FMLM_TRACE

@@ -181,7 +181,7 @@ def _packed_launch(*, q_view, k_view, v_view, q_layout, kv_layout, seq_len, tota
         # A repeated call with the same offsets tensors reuses its device tile
         # schedule instead of rebuilding it.
         key_tensors = (cu_seqlens_q, ctx.cu_seqlens_kv) if has_ctx else (cu_seqlens_q,)
-        key_scalars = (device.type, device.index, d, batch, total_q_len, int(has_ctx), int(causal),
+        key_scalars = (device.type, device.index, d, batch, num_heads, total_q_len, int(has_ctx), int(causal),
                        int(ctx.context_batch_size) if has_ctx else 0)
         ws, cached = cache.packing.schedule_workspace(key_tensors, key_scalars, nbytes, device)
         args.reuse_schedule = int(cached)

@@ -459,6 +459,37 @@ def test_large_logits_rescale_path():
     no_device_errors()
 
 
+# ----------------------------------------------------------------- head_dim 128, both item granularities
+# At head_dim 128 a problem with fewer 256-row tile pairs than SMs runs one
+# 128-row tile per work item; larger ones run two tiles per item.  Small and
+# large problems exercise both.
+
+
+@pytest.mark.parametrize("B,H", [(2, 3), (16, 16)])
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float16])
+def test_head_dim_128_both_item_sizes(B, H, dt):
+    g = torch.Generator().manual_seed(128 + B + H)
+    N, D = 256, 128
+    lengths = torch.randint(1, N + 1, (B,), generator=g, dtype=torch.int32)
+    q, k, v = (_rand((B, H, N, D), dt, g) for _ in range(3))
+    ctx = torch.randint(0, 200, (B,), generator=g, dtype=torch.int32)
+    cu_kv = torch.cat([torch.zeros(1, dtype=torch.int32), ctx.cumsum(0).to(torch.int32)])
+    tcl = int(cu_kv[-1])
+    kc, vc = (_rand((H * tcl, D), dt, g) for _ in range(2))
+    cache = fm().InferenceCache()
+    cache.prefill_kv_cache(0, k_cache=kc.to(DEV), v_cache=vc.to(DEV), total_context_len=tcl,
+                           cu_seqlens_kv=cu_kv.to(DEV), context_batch_size=B, is_mla=False, num_heads=H, head_dim=D)
+    meta = fm().build_pack_metadata(lengths.to(DEV), N, 64)
+    out = fm().flash_attn_mlm_compressed(q.to(DEV), k.to(DEV), v.to(DEV), num_heads=H, q_meta=meta,
+                                         scale=D ** -0.5, inference_cache=cache, layer_id=0, block_n=64)
+    ref = oracle.attention_packed(q.float().numpy(), k.float().numpy(), v.float().numpy(),
+                                  meta.cu_seqlens.cpu().numpy(), D ** -0.5, k_cache=kc.float().numpy(),
+                                  v_cache=vc.float().numpy(), cu_kv=cu_kv.numpy(), context_batch_size=B,
+                                  total_context_len=tcl)
+    assert_close_tol(out, ref, dt, f"D=128 B={B} H={H}")
+    no_device_errors()
+
+
 # ----------------------------------------------------------------- long per-sequence contexts
 # Few work items, each walking a long context (up to 47 key blocks) then its
 # own tokens; two identical calls must give bit-identical outputs.
