@@ -223,11 +223,13 @@ class Workload:
     def launches_per_step(self):
         if self.dense:
             return 1
-        n = 2  # schedule + attention
+        # The tile schedule is built on the first call with a given metadata
+        # and memoised in the InferenceCache, so a timed step launches only:
+        n = 1  # attention
         if self.causal:
             n += 2  # pack main K and V into the packed prefix
         if self.prefill_lengths is not None:
-            n += 2 + 2  # prefill: pack K, V into the cache + schedule + attention
+            n += 2 + 1  # prefill: pack K, V into the cache + attention
         return n
 
     # ---------------------------------------------------------------- CPU oracle sample
