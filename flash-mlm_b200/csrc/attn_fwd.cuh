@@ -31,7 +31,7 @@
 namespace fmlm {
 
 // Error codes written to the device error word.
-enum : int { kErrTimeout = 1, kErrSmemAlign = 2 };
+enum : int { kErrTimeout = 1, kErrSmemAlign = 2, kErrContextIndex = 3 };
 
 // Packed-mode workspace (int32): [0] entry count, [1] next-item counter,
 // [2] CTAs finished, [3] unused, then one (b << 16 | pair) entry per query
@@ -54,6 +54,7 @@ struct AttnParams {
   float scale_log2; // scale * log2(e)
   const int* cu_q;  // [B+1] packed query offsets
   const int* cu_kv; // context offsets (packed)
+  const int* ctx_index;  // packed, optional: context entry of each query batch
   int* work;        // packed: schedule workspace (layout at kWorkHeader)
   void* out;        // [rows, D]
   int* err;         // device error word
@@ -256,8 +257,13 @@ __device__ __forceinline__ Item decode_item(const AttnParams& p, int w) {
   } else if (p.mode == 0) {
     c.b = (p.ctx_bs > 1) ? b : 0; c.row0 = 0; c.row1 = p.ctx_len;
   } else {
-    const int ci = (p.ctx_bs > 1) ? b : 0;
-    c.b = 0; c.row0 = __ldg(p.cu_kv + ci); c.row1 = __ldg(p.cu_kv + ci + 1);
+    const int ci = p.ctx_index ? __ldg(p.ctx_index + b) : (p.ctx_bs > 1) ? b : 0;
+    if (ci < 0 || ci >= p.ctx_bs) {
+      atomicExch(p.err, kErrContextIndex);  // attend no context
+      c.b = 0; c.row0 = 0; c.row1 = 0;
+    } else {
+      c.b = 0; c.row0 = __ldg(p.cu_kv + ci); c.row1 = __ldg(p.cu_kv + ci + 1);
+    }
   }
   // main segment
   Seg& m = it.main;

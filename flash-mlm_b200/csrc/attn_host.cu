@@ -94,13 +94,13 @@ int encode_view(CUtensorMap* m, const fmlm_view4& v, int D, int box_rows, int dt
 constexpr int kSchedThreads = 1024;
 constexpr int kSortMax = 2048;
 
-__device__ __forceinline__ int seq_key_rows(const int* cu_q, const int* cu_kv, int b, int ctx_bs, int has_ctx,
-                                            int causal) {
+__device__ __forceinline__ int seq_key_rows(const int* cu_q, const int* cu_kv, const int* ctx_index, int b,
+                                            int ctx_bs, int has_ctx, int causal) {
   const int L = cu_q[b + 1] - cu_q[b];
   int kv = causal ? cu_q[b + 1] : L;
   if (has_ctx) {
-    const int c = ctx_bs > 1 ? b : 0;
-    kv += cu_kv[c + 1] - cu_kv[c];
+    const int c = ctx_index ? ctx_index[b] : ctx_bs > 1 ? b : 0;
+    if (c >= 0 && c < ctx_bs) kv += cu_kv[c + 1] - cu_kv[c];
   }
   return kv;
 }
@@ -134,7 +134,8 @@ __device__ int block_exclusive_scan(int v, int* warp_sums, int* total) {
 }
 
 __global__ void __launch_bounds__(kSchedThreads) sched_kernel(const int* __restrict__ cu_q,
-                                                              const int* __restrict__ cu_kv, int B, int ctx_bs,
+                                                              const int* __restrict__ cu_kv,
+                                                              const int* __restrict__ ctx_index, int B, int ctx_bs,
                                                               int has_ctx, int causal, int pair, int* work,
                                                               int cap) {
   __shared__ int key[kSortMax];
@@ -145,7 +146,7 @@ __global__ void __launch_bounds__(kSchedThreads) sched_kernel(const int* __restr
   const bool sort = B <= kSortMax;
   if (threadIdx.x == 0) running = 0;
   if (sort) {
-    for (int b = threadIdx.x; b < B; b += blockDim.x) key[b] = seq_key_rows(cu_q, cu_kv, b, ctx_bs, has_ctx, causal);
+    for (int b = threadIdx.x; b < B; b += blockDim.x) key[b] = seq_key_rows(cu_q, cu_kv, ctx_index, b, ctx_bs, has_ctx, causal);
     __syncthreads();
     for (int b = threadIdx.x; b < B; b += blockDim.x) {
       const int kb = key[b];
@@ -339,8 +340,10 @@ extern "C" int fmlm_attn_packed_fwd(const fmlm_packed_args* a, void* stream) {
   if ((int64_t)a->seq_len > 65535LL * pair_rows(D)) return set_error(FMLM_ERR_INVALID, "sequence too long");
   const bool has_ctx = !a->prefill && a->cu_seqlens_kv != nullptr && a->k_cache.data != nullptr &&
                        a->k_cache.rows > 0;
-  if (has_ctx && a->context_batch_size > 1 && a->context_batch_size < a->batch)
+  const int32_t* ctx_index = has_ctx ? a->context_index : nullptr;
+  if (has_ctx && !ctx_index && a->context_batch_size > 1 && a->context_batch_size < a->batch)
     return set_error(FMLM_ERR_INVALID, "context_batch_size (%d) must be 1 or >= batch (%d)", a->context_batch_size, a->batch);
+  if (ctx_index && a->context_batch_size < 1) return set_error(FMLM_ERR_INVALID, "context_batch_size must be >= 1");
   const size_t need = fmlm_packed_workspace_bytes(a->batch, a->total_q_len, D);
   if (!a->workspace || a->workspace_bytes < need || !aligned16(a->workspace))
     return set_error(FMLM_ERR_INVALID, "workspace too small (%zu bytes needed)", need);
@@ -363,7 +366,7 @@ extern "C" int fmlm_attn_packed_fwd(const fmlm_packed_args* a, void* stream) {
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (!a->reuse_schedule) {
     sched_kernel<<<1, kSchedThreads, 0, s>>>(a->cu_seqlens_q, has_ctx ? a->cu_seqlens_kv : a->cu_seqlens_q,
-                                             a->batch, a->context_batch_size, has_ctx, a->causal_query_seq_attn, pr,
+                                             ctx_index, a->batch, a->context_batch_size, has_ctx, a->causal_query_seq_attn, pr,
                                              work, (int)cap);
     if ((rc = check_launch("sched_kernel"))) return rc;
   }
@@ -381,6 +384,7 @@ extern "C" int fmlm_attn_packed_fwd(const fmlm_packed_args* a, void* stream) {
   p.scale_log2 = a->scale * 1.4426950408889634f;
   p.cu_q = a->cu_seqlens_q;
   p.cu_kv = has_ctx ? a->cu_seqlens_kv : a->cu_seqlens_q;
+  p.ctx_index = ctx_index;
   p.work = work;
   p.out = a->out;
   p.err = a->error_word;

@@ -84,6 +84,7 @@ class PackedArgs(ctypes.Structure):
         ("workspace_bytes", ctypes.c_size_t),
         ("error_word", ctypes.c_void_p),
         ("reuse_schedule", ctypes.c_int32),
+        ("context_index", ctypes.c_void_p),
     ]
 
 

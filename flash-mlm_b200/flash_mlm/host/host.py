@@ -148,7 +148,8 @@ def flash_attn_mlm(
 
 
 def _packed_launch(*, q_view, k_view, v_view, q_layout, kv_layout, seq_len, total_q_len, num_heads, batch, d,
-                   dtype, is_mla, prefill, causal, ctx, scale, cu_seqlens_q, out, out_rows_per_head, cache, device):
+                   dtype, is_mla, prefill, causal, ctx, scale, cu_seqlens_q, out, out_rows_per_head, cache, device,
+                   context_index=None):
     total_context_len = int(ctx.total_context_len)
     has_ctx = (not prefill) and total_context_len > 0
     ctx_heads = 1 if is_mla else num_heads
@@ -172,6 +173,8 @@ def _packed_launch(*, q_view, k_view, v_view, q_layout, kv_layout, seq_len, tota
         args.k_cache = _cache_view(kc, ctx_heads, total_context_len, 1)
         args.v_cache = _cache_view(vc, ctx_heads, total_context_len, 1)
         args.cu_seqlens_kv = ctx.cu_seqlens_kv.contiguous().data_ptr()
+        if context_index is not None:
+            args.context_index = context_index.data_ptr()
     args.cu_seqlens_q = cu_seqlens_q.data_ptr()
     args.out = out.data_ptr()
     args.out_rows_per_head = out_rows_per_head
@@ -181,7 +184,10 @@ def _packed_launch(*, q_view, k_view, v_view, q_layout, kv_layout, seq_len, tota
         # A repeated call with the same offsets tensors reuses its device tile
         # schedule instead of rebuilding it.
         key_tensors = (cu_seqlens_q, ctx.cu_seqlens_kv) if has_ctx else (cu_seqlens_q,)
+        if has_ctx and context_index is not None:
+            key_tensors = key_tensors + (context_index,)
         key_scalars = (device.type, device.index, d, batch, num_heads, total_q_len, int(has_ctx), int(causal),
+                       context_index is not None,
                        int(ctx.context_batch_size) if has_ctx else 0)
         ws, cached = cache.packing.schedule_workspace(key_tensors, key_scalars, nbytes, device)
         args.reuse_schedule = int(cached)
@@ -219,6 +225,7 @@ def flash_attn_mlm_compressed(
     auto_tune_tiles: bool = False,
     prefill: bool = False,
     causal_query_seq_attn: bool = False,
+    context_index: torch.Tensor | None = None,
 ) -> torch.Tensor:
     """Packed variable-length MLM attention.
 
@@ -230,6 +237,13 @@ def flash_attn_mlm_compressed(
     ``k[:, 0]`` as both key and value.  With ``prefill=True`` the context is
     skipped and this call's packed, padded K/V become the layer's context
     (``cu_seqlens_kv`` = ``q_meta.cu_seqlens``).
+
+    ``context_index`` (optional, int32 [B] on q's device) maps query sequence
+    b to context entry ``context_index[b]`` of the cached layer (index-mapped
+    context batching, listed as planned in the reference README): any number
+    of query sequences may share any entry.  It needs a cached context, is not
+    combined with ``prefill`` or an explicit ``context_batch_size``, and costs
+    one device read to range-check the indices.
 
     Returns the packed output [H * total_tokens, D] in q's dtype.
     """
@@ -243,6 +257,18 @@ def flash_attn_mlm_compressed(
     if q_meta.batch_ids_block_n != block_n:
         raise ValueError("q_meta was built with different block_n")
     cu_seqlens_q = q_meta.cu_seqlens
+    if context_index is not None:
+        if prefill:
+            raise ValueError("context_index cannot be combined with prefill=True")
+        if inference_cache is None:
+            raise ValueError("context_index requires inference_cache and layer_id")
+        if context_batch_size is not None:
+            raise ValueError("context_index selects context entries itself; leave context_batch_size unset")
+        if (not isinstance(context_index, torch.Tensor) or context_index.dtype != torch.int32
+                or tuple(context_index.shape) != (b,)):
+            raise ValueError("context_index must be an int32 tensor of shape [B]")
+        if context_index.device != q.device:
+            raise ValueError("context_index must be on q's device")
 
     use_layer_cache = inference_cache is not None
     ctx = _maybe_get_cache_context(inference_cache=inference_cache, layer_id=layer_id, batch_size=b, is_mla=is_mla,
@@ -261,6 +287,11 @@ def flash_attn_mlm_compressed(
         raise ValueError("context_batch_size must be >= 1")
     if ctx.context_batch_size + 1 > ctx.cu_seqlens_kv.numel():
         raise ValueError("context_batch_size is incompatible with cu_seqlens_kv length")
+    if context_index is not None and int(ctx.total_context_len) > 0:
+        lo, hi = (int(x) for x in torch.stack(torch.aminmax(context_index)).tolist())
+        if lo < 0 or hi >= ctx.context_batch_size:
+            raise ValueError(f"context_index values must lie in [0, {ctx.context_batch_size})")
+        context_index = context_index.contiguous()
 
     cu_seqlens_q = cu_seqlens_q.contiguous()
     k_main = k[:, :1] if is_mla else k
@@ -303,7 +334,8 @@ def flash_attn_mlm_compressed(
                           kv_layout=kv_layout, seq_len=n, total_q_len=max(kv_rows, total_tokens),
                           num_heads=num_heads, batch=b, d=d, dtype=q.dtype, is_mla=is_mla, prefill=prefill,
                           causal=causal_query_seq_attn, ctx=ctx, scale=scale, cu_seqlens_q=cu_seqlens_q, out=out,
-                          out_rows_per_head=total_tokens, cache=inference_cache, device=q.device)
+                          out_rows_per_head=total_tokens, cache=inference_cache, device=q.device,
+                          context_index=context_index)
     del keep
     return out
 

@@ -98,6 +98,11 @@ typedef struct fmlm_packed_args {
   int32_t* error_word;
   int32_t reuse_schedule;           /* 1: the workspace already holds the tile schedule of an earlier call
                                        with the same cu_seqlens / context / flags; skip rebuilding it */
+  const int32_t* context_index;     /* optional [batch] (device): query batch b attends context entry
+                                       context_index[b] (0 <= index < context_batch_size); NULL: the
+                                       context_batch_size rule.  An index out of range attends no context
+                                       and sets the error word.  No counterpart in the reference, whose
+                                       README lists index-mapped context batching as planned. */
 } fmlm_packed_args;
 
 /* Dense bidirectional attention over [context ++ own sequence]. */

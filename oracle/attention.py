@@ -26,14 +26,16 @@ def _softmax_attend(q: np.ndarray, k: np.ndarray, v: np.ndarray, scale: float) -
 
 
 def attention_packed(q, k, v, cu_q, scale, *, k_cache=None, v_cache=None, cu_kv=None, context_batch_size=1,
-                     total_context_len=0, is_mla=False, causal_query_seq_attn=False, prefill=False) -> np.ndarray:
+                     total_context_len=0, is_mla=False, causal_query_seq_attn=False, prefill=False,
+                     context_index=None) -> np.ndarray:
     """Packed varlen attention.  q/k/v padded [B,H,N,D]; returns packed [H*T, D].
 
     Query b (tokens [0, L_b)) attends to context rows [cu_kv[c], cu_kv[c+1])
     (c = b if context_batch_size > 1 else 0; head-offset h*total_context_len
     unless MLA; skipped when prefill) followed by its own tokens, or with
     causal_query_seq_attn by all tokens of sequences 0..b.  MLA keys and
-    values are k[:, 0].
+    values are k[:, 0].  ``context_index`` (no counterpart in the reference,
+    whose README plans it) replaces the choice of c: c = context_index[b].
     """
     B, H, N, D = q.shape
     cu = [int(x) for x in cu_q]
@@ -44,7 +46,7 @@ def attention_packed(q, k, v, cu_q, scale, *, k_cache=None, v_cache=None, cu_kv=
         if L == 0:
             continue
         if not prefill and cu_kv is not None and k_cache is not None and total_context_len > 0:
-            c = b if context_batch_size > 1 else 0
+            c = int(context_index[b]) if context_index is not None else (b if context_batch_size > 1 else 0)
             c0, c1 = int(cu_kv[c]), int(cu_kv[c + 1])
         else:
             c0 = c1 = 0

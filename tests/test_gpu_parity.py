@@ -459,6 +459,68 @@ def test_large_logits_rescale_path():
     no_device_errors()
 
 
+# ----------------------------------------------------------------- index-mapped context (no reference counterpart)
+# Query sequence b attends context entry context_index[b]; several sequences
+# share entries and the entry count differs from the batch size.
+
+
+@pytest.mark.parametrize("D,dt,is_mla", [(64, torch.bfloat16, False), (128, torch.float16, False),
+                                         (512, torch.bfloat16, True)])
+def test_context_index_vs_oracle(D, dt, is_mla):
+    g = torch.Generator().manual_seed(77 + D)
+    B, H, N = 5, 1 if is_mla else 3, 130
+    lengths = torch.tensor([130, 17, 64, 1, 99], dtype=torch.int32)
+    q = _rand((B, H, N, D), dt, g, 0.5)
+    k = _rand((B, 1 if is_mla else H, N, D), dt, g, 0.5).expand(B, H, N, D) if is_mla else _rand((B, H, N, D), dt, g)
+    v = k if is_mla else _rand((B, H, N, D), dt, g)
+    ctx = torch.tensor([300, 0, 129], dtype=torch.int32)  # three entries, one empty
+    cu_kv = torch.cat([torch.zeros(1, dtype=torch.int32), ctx.cumsum(0).to(torch.int32)])
+    tcl = int(cu_kv[-1])
+    rows = tcl if is_mla else H * tcl
+    kc = _rand((rows, D), dt, g, 0.5)
+    vc = kc if is_mla else _rand((rows, D), dt, g)
+    index = torch.tensor([2, 0, 2, 1, 0], dtype=torch.int32)
+    cache = fm().InferenceCache()
+    cache.prefill_kv_cache(0, k_cache=kc.to(DEV), v_cache=None if is_mla else vc.to(DEV), total_context_len=tcl,
+                           cu_seqlens_kv=cu_kv.to(DEV), context_batch_size=3, is_mla=is_mla, num_heads=H, head_dim=D)
+    meta = fm().build_pack_metadata(lengths.to(DEV), N, 32)
+    scale = D ** -0.5
+    out = fm().flash_attn_mlm_compressed(q.to(DEV), k.to(DEV), v.to(DEV), num_heads=H, q_meta=meta, scale=scale,
+                                         inference_cache=cache, layer_id=0, is_mla=is_mla,
+                                         context_index=index.to(DEV))
+    ref = oracle.attention_packed(q.float().numpy(), k.float().numpy(), v.float().numpy(),
+                                  meta.cu_seqlens.cpu().numpy(), scale, k_cache=kc.float().numpy(),
+                                  v_cache=vc.float().numpy(), cu_kv=cu_kv.numpy(), context_batch_size=3,
+                                  total_context_len=tcl, is_mla=is_mla, context_index=index.numpy())
+    assert_close_tol(out, ref, dt, f"context_index D={D}")
+    no_device_errors()
+
+
+def test_context_index_rejections():
+    g = torch.Generator().manual_seed(5)
+    B, H, N, D = 2, 2, 16, 64
+    q = _rand((B, H, N, D), torch.float16, g).to(DEV)
+    cache = fm().InferenceCache()
+    kc = _rand((H * 8, D), torch.float16, g).to(DEV)
+    cache.prefill_kv_cache(0, k_cache=kc, v_cache=kc.clone(), total_context_len=8,
+                           cu_seqlens_kv=torch.tensor([0, 5, 8], dtype=torch.int32, device=DEV),
+                           context_batch_size=2, is_mla=False, num_heads=H, head_dim=D)
+    meta = fm().build_pack_metadata(torch.tensor([16, 9], dtype=torch.int32, device=DEV), N, 32)
+    call = lambda **kw: fm().flash_attn_mlm_compressed(q, q, q, num_heads=H, q_meta=meta, scale=0.125, **kw)
+    idx = torch.tensor([1, 0], dtype=torch.int32, device=DEV)
+    with pytest.raises(ValueError, match="requires inference_cache"):
+        call(context_index=idx)
+    with pytest.raises(ValueError, match="shape \\[B\\]"):
+        call(inference_cache=cache, layer_id=0, context_index=idx.long())
+    with pytest.raises(ValueError, match="lie in \\[0, 2\\)"):
+        call(inference_cache=cache, layer_id=0, context_index=torch.tensor([1, 2], dtype=torch.int32, device=DEV))
+    with pytest.raises(ValueError, match="prefill"):
+        call(inference_cache=cache, layer_id=1, context_index=idx, prefill=True)
+    with pytest.raises(ValueError, match="leave context_batch_size unset"):
+        call(inference_cache=cache, layer_id=0, context_index=idx, context_batch_size=2)
+    no_device_errors()
+
+
 # ----------------------------------------------------------------- head_dim 128, both item granularities
 # At head_dim 128 a problem with fewer 256-row tile pairs than SMs runs one
 # 128-row tile per work item; larger ones run two tiles per item.  Small and
