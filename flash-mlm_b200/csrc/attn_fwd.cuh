@@ -118,14 +118,24 @@ struct AttnCfg {
 #ifndef FMLM_MLA_BN
 #define FMLM_MLA_BN 48
 #endif
-  static constexpr int BN = (D == 512) ? (TQ ? FMLM_MLA_BN : 32) : (D >= 256) ? 64 : (D == 128) ? FMLM_BN_D128 : 128;  // key rows per block
+#ifndef FMLM_MLA_KSPLIT
+#define FMLM_MLA_KSPLIT 1
+#endif
+  // KSPLIT (with TQ): the K tile is held as two 256-column halves in two
+  // rings.  The half this item uses as V (columns dh*DV ...) stays until PV;
+  // the other half is needed only by S and is released as soon as S has run,
+  // so a shorter ring suffices and 64-key blocks fit in shared memory.
+  static constexpr bool KSPLIT = TQ && FMLM_MLA_KSPLIT;
+  static constexpr int BN = (D == 512) ? (KSPLIT ? 64 : TQ ? FMLM_MLA_BN : 32) : (D >= 256) ? 64 : (D == 128) ? FMLM_BN_D128 : 128;  // key rows per block
   static constexpr int PAIR = NQ * BM;             // query rows per work item
   static constexpr int SWB = (D * 2 >= 128) ? 128 : D * 2;  // swizzle span in bytes
   static constexpr int SLAB_COLS = SWB / 2;
   static constexpr int NSLAB = D / SLAB_COLS;
   static constexpr int Q_BYTES = BM * QS * 2;
   static constexpr int Q_NSLAB = QS / SLAB_COLS;
-  static constexpr int KV_BYTES = BN * D * 2;
+  static constexpr int KV_BYTES = KSPLIT ? BN * (D / 2) * 2 : BN * D * 2;  // KSPLIT: one half tile
+  static constexpr int KNSLAB = KSPLIT ? NSLAB / 2 : NSLAB;  // swizzle slabs per K/V tile in shared memory
+  static constexpr int SHORT_STAGES = KSPLIT ? 2 : 0;        // KSPLIT: ring of the halves used by S only
   // One tile per CTA at D <= 64 runs two CTAs per SM (TMEM 256 columns and
   // about 80 KB of shared memory each): the two CTAs work on independent items.
   static constexpr int CTAS_PER_SM = (NQ == 1 && D <= 64) ? 2 : 1;
@@ -141,7 +151,7 @@ struct AttnCfg {
   // Q buffers: with two, the next item's Q is loaded while the current item
   // still computes, so its first S is ready when the softmax reaches it.
   static constexpr int QBUF = (CTAS_PER_SM == 2) ? FMLM_QBUF_2CTA : 1;
-  static constexpr int STAGES = (CTAS_PER_SM == 2) ? (QBUF == 2 ? 2 : FMLM_STAGES_2CTA) : (D <= 32) ? 4 : (D <= 64) ? 3 : (D == 512) ? (TQ ? (BN <= 48 ? 3 : 2) : 3)
+  static constexpr int STAGES = (CTAS_PER_SM == 2) ? (QBUF == 2 ? 2 : FMLM_STAGES_2CTA) : (D <= 32) ? 4 : (D <= 64) ? 3 : (D == 512) ? ((TQ && !KSPLIT) ? (BN <= 48 ? 3 : 2) : 3)
                               : (D == 128 && BN == 64) ? 4 : 2;
   static constexpr int NUM_SOFTMAX_WARPS = 4 * NQ;
   static constexpr int TMA_WARP = NUM_SOFTMAX_WARPS;
@@ -173,7 +183,7 @@ struct AttnCfg {
   static constexpr int TMEM_COLS = TMEM_USED <= 32 ? 32 : TMEM_USED <= 64 ? 64 : TMEM_USED <= 128 ? 128
                                  : TMEM_USED <= 256 ? 256 : 512;
   static_assert(TMEM_USED <= 512, "TMEM budget");
-  static constexpr int SMEM_TILES = QBUF * NQ * Q_BYTES + (MLA_ONLY ? 1 : 2) * STAGES * KV_BYTES;
+  static constexpr int SMEM_TILES = QBUF * NQ * Q_BYTES + (MLA_ONLY ? 1 : 2) * STAGES * KV_BYTES + SHORT_STAGES * KV_BYTES;
   // Two CTAs with three K/V stages need all but 1.5 KB of the SM's 228 KB, so
   // they carry no alignment slack: the dynamic shared window of a kernel with
   // no static shared memory starts 1024-byte aligned, which the kernel checks.
@@ -292,6 +302,7 @@ struct __align__(8) AttnBarriers {
   int item_idx[4];
   uint64_t exp_tok[2];  // two-tile ping-pong: tile t may run its exp2 loop
   uint64_t q1_full;     // TQ: the softmax warps have written this item's Q columns [QS, D) to TMEM
+  uint64_t ks_empty[2]; // KSPLIT: short-ring slot free (the S that read it has completed); v_full is its "full"
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -324,7 +335,8 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
   uint8_t* sQ = smem;
   uint8_t* sK = sQ + C::QBUF * NQ * C::Q_BYTES;
   uint8_t* sV = C::MLA_ONLY ? sK : sK + STAGES * C::KV_BYTES;
-  AttnBarriers* bar = reinterpret_cast<AttnBarriers*>(sV + STAGES * C::KV_BYTES);
+  uint8_t* sKs = sK + STAGES * C::KV_BYTES;  // KSPLIT short ring (SHORT_STAGES half tiles)
+  AttnBarriers* bar = reinterpret_cast<AttnBarriers*>(sV + STAGES * C::KV_BYTES + C::SHORT_STAGES * C::KV_BYTES);
   volatile int* abort_flag = &bar->abort_flag;
   Item* item_ring = reinterpret_cast<Item*>(reinterpret_cast<uint8_t*>(bar) + 512);
 
@@ -374,6 +386,8 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
       mbar_init(&bar->item_empty[i], 5 * NQ);  // every MMA and softmax warp
     }
     mbar_init(&bar->q1_full, 4);
+    mbar_init(&bar->ks_empty[0], 1);
+    mbar_init(&bar->ks_empty[1], 1);
     mbar_init(&bar->exp_tok[0], 4);
     mbar_init(&bar->exp_tok[1], 4);
     bar->abort_flag = 0;
@@ -440,7 +454,7 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
       failed = __any_sync(0xffffffffu, failed);
       if (!failed) {
         const int nbytes = (BN - pend_valid) * SWB;
-        for (int s = 0; s < C::NSLAB; ++s) {
+        for (int s = 0; s < C::KNSLAB; ++s) {
           uint4* z = reinterpret_cast<uint4*>(pend_tile + s * (BN * SWB) + pend_valid * SWB);
           for (int i = lane; i < nbytes / 16; i += 32) z[i] = make_uint4(0, 0, 0, 0);
         }
@@ -517,10 +531,27 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
           uint8_t* tv = sV + st * C::KV_BYTES;
           resolve_fix();
           if (!mbar_wait(&bar->kv_empty[st], ph ^ 1u, abort_flag, tmo)) fail();
+          const int ss = fill % 2;
+          if constexpr (C::KSPLIT) {
+            if (!mbar_wait(&bar->ks_empty[ss], ((fill / 2) & 1u) ^ 1u, abort_flag, tmo)) fail();
+          }
           failed = __any_sync(0xffffffffu, failed);
           if (lane == 0) {
             FMLM_TR(40);
-            if (!failed) {
+            if (!failed && C::KSPLIT) {
+              // long ring: the half this item uses as V (columns dh*256...);
+              // short ring: the other half, read only by S.
+              const int hl = it.dh, hs = 1 - it.dh;
+              uint64_t* lb = fix ? &bar->fix : &bar->k_full[st];
+              mbar_arrive_expect_tx(lb, C::KV_BYTES);
+              for (int s = 0; s < C::KNSLAB; ++s)
+                tma_load_4d(tk + s * (BN * SWB), mk, lb, (hl * C::KNSLAB + s) * C::SLAB_COLS, row, sgm.h, sgm.b);
+              uint8_t* ts = sKs + ss * C::KV_BYTES;
+              mbar_arrive_expect_tx(&bar->v_full[ss], C::KV_BYTES);
+              for (int s = 0; s < C::KNSLAB; ++s)
+                tma_load_4d(ts + s * (BN * SWB), mk, &bar->v_full[ss], (hs * C::KNSLAB + s) * C::SLAB_COLS, row, sgm.h,
+                            sgm.b);
+            } else if (!failed) {
               if (!(fix && mla)) {
                 mbar_arrive_expect_tx(&bar->k_full[st], C::KV_BYTES);
                 for (int s = 0; s < C::NSLAB; ++s)
@@ -574,7 +605,7 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
     constexpr uint32_t idesc_qk = make_idesc_f16(fmt, 0, 0, BM, BN);
     constexpr uint32_t idesc_pv = make_idesc_f16(fmt, 0, 1, BM, C::DV);
     constexpr uint32_t layout = swizzle_code(SWB);
-    const uint32_t sQ0 = smem_u32(sQ) + t * C::Q_BYTES, sKa = smem_u32(sK), sVa = smem_u32(sV);
+    const uint32_t sQ0 = smem_u32(sQ) + t * C::Q_BYTES, sKa = smem_u32(sK), sVa = smem_u32(sV), sKsa = smem_u32(sKs);
     uint32_t sQa = sQ0;  // this item's Q buffer
     const uint32_t tS_d = tmem_base + C::TM_S + t * BN;
     const uint32_t tO_d = tmem_base + C::TM_O + t * C::DV;
@@ -585,12 +616,20 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
     bool first_item = true;
     uint32_t fill = 0;
 
-    auto issue_s = [&](int st, uint32_t d_col = 0) {
+    // KSPLIT: K columns [0, 256) come from the long ring when dh == 0 and from
+    // the short ring (slot ss) otherwise, columns [256, 512) the other way round.
+    auto issue_s = [&](int st, uint32_t d_col = 0, int ss = 0, int dh = 0) {
       if (leader) {
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t slab = (kk * 32) / SWB, inrow = (kk * 32) % SWB;
-          const uint64_t b = make_smem_desc(sKa + st * C::KV_BYTES + slab * (BN * SWB) + inrow, 16, 8 * SWB, layout);
+          uint32_t kbase = sKa + st * C::KV_BYTES + slab * (BN * SWB);
+          if constexpr (C::KSPLIT) {
+            const int half = kk / (D / 32);
+            const uint32_t kslab = slab - half * C::KNSLAB;
+            kbase = (half == dh ? sKa + st * C::KV_BYTES : sKsa + ss * C::KV_BYTES) + kslab * (BN * SWB);
+          }
+          const uint64_t b = make_smem_desc(kbase + inrow, 16, 8 * SWB, layout);
           if (C::TQ && kk >= C::QS / 16) {
             umma_ts(tS_d + d_col, tmem_base + C::TM_Q1 + (kk - C::QS / 16) * 8, b, idesc_qk, 1u);
           } else {
@@ -603,7 +642,8 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
     auto issue_pv = [&](int st, bool acc, int dh, uint32_t p_col = 0) {
       if (leader) {
         // V columns [dh*DV, dh*DV + DV) start at slab dh*DV/SLAB_COLS of the tile.
-        const uint32_t vbase = (mla ? sKa : sVa) + st * C::KV_BYTES + (dh * C::DV / C::SLAB_COLS) * (BN * SWB);
+        const uint32_t vbase = C::KSPLIT ? sKa + st * C::KV_BYTES  // the long ring holds exactly the V half
+                               : (mla ? sKa : sVa) + st * C::KV_BYTES + (dh * C::DV / C::SLAB_COLS) * (BN * SWB);
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk) {
           const uint64_t b = make_smem_desc(vbase + kk * 16 * SWB, BN * SWB, 8 * SWB, layout);
@@ -652,14 +692,19 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
             const uint32_t g1 = gb + j + 1;
             const int st1 = (fill + j + 1) % STAGES;
             if (!wait(&bar->k_full[st1], ((fill + j + 1) / STAGES) & 1u)) { ok = false; break; }
+            const int ss1 = (fill + j + 1) % 2;
+            if constexpr (C::KSPLIT) {
+              if (!wait(&bar->v_full[ss1], ((fill + j + 1) / 2) & 1u)) { ok = false; break; }
+            }
             if (j < 0) {
               // the softmax warps' copy of this item's Q columns [QS, D) into TMEM
               if (!wait(&bar->q1_full, q1_ph)) { ok = false; break; }
               q1_ph ^= 1u;
             }
             tc_fence_after();
-            issue_s(st1, (g1 & 1u) * BN);
+            issue_s(st1, (g1 & 1u) * BN, ss1, it.dh);
             commit(&bar->s_full[g1 & 1u]);
+            if constexpr (C::KSPLIT) commit(&bar->ks_empty[ss1]);
             FMLM_TR(32);
             if (j + 2 == nb) commit(q_empty);
           }
