@@ -31,7 +31,7 @@
 namespace fmlm {
 
 // Error codes written to the device error word.
-enum : int { kErrTimeout = 1, kErrSmemAlign = 2, kErrContextIndex = 3 };
+enum : int { kErrTimeout = 1, kErrSmemAlign = 2, kErrContextIndex = 3, kErrSeqTooLong = 4 };
 
 // Packed-mode workspace (int32): [0] entry count, [1] next-item counter,
 // [2] CTAs finished, [3] unused, then one (b << 16 | pair) entry per query

@@ -137,7 +137,7 @@ __global__ void __launch_bounds__(kSchedThreads) sched_kernel(const int* __restr
                                                               const int* __restrict__ cu_kv,
                                                               const int* __restrict__ ctx_index, int B, int ctx_bs,
                                                               int has_ctx, int causal, int pair, int* work,
-                                                              int cap) {
+                                                              int cap, int* err) {
   __shared__ int key[kSortMax];
   __shared__ int order[kSortMax];
   __shared__ int warp_sums[32];
@@ -162,7 +162,13 @@ __global__ void __launch_bounds__(kSchedThreads) sched_kernel(const int* __restr
   for (int base = 0; base < B; base += blockDim.x) {
     const int s = base + threadIdx.x;
     const int b = s < B ? (sort ? order[s] : s) : -1;
-    const int n = b >= 0 ? (cu_q[b + 1] - cu_q[b] + pair - 1) / pair : 0;
+    int n = b >= 0 ? (cu_q[b + 1] - cu_q[b] + pair - 1) / pair : 0;
+    // A work entry keeps the item's index within its sequence in 16 bits:
+    // a longer sequence is not scheduled and the call reports the error.
+    if (n > 65536) {
+      atomicExch(err, kErrSeqTooLong);
+      n = 0;
+    }
     const int ex = block_exclusive_scan(n, warp_sums, &total);
     const int off = running;
     for (int i = 0; i < n; ++i) {
@@ -330,6 +336,11 @@ extern "C" int fmlm_attn_packed_fwd(const fmlm_packed_args* a, void* stream) {
   if (D == 512 && !a->is_mla) return set_error(FMLM_ERR_UNSUPPORTED, "HEAD_DIM 512 is supported for MLA only");
   if (a->batch <= 0 || a->num_heads <= 0) return set_error(FMLM_ERR_INVALID, "bad batch / num_heads");
   if (a->batch >= 32768) return set_error(FMLM_ERR_INVALID, "batch must be < 32768");
+  if (a->total_q_len < 0) return set_error(FMLM_ERR_INVALID, "total_q_len must be >= 0");
+  if (a->total_q_len > 0x7fff0000LL) return set_error(FMLM_ERR_INVALID, "total_q_len must be < 2^31 - 2^16");
+  // Work entries hold the 128-row tile index of a sequence in 16 bits.
+  if (a->q_layout != FMLM_LAYOUT_PADDED && a->total_q_len / 128 > 65535)
+    return set_error(FMLM_ERR_INVALID, "packed q: total_q_len must be below 65536 * 128 rows per head");
   if (!a->cu_seqlens_q) return set_error(FMLM_ERR_INVALID, "cu_seqlens_q is required");
   if (!a->error_word) return set_error(FMLM_ERR_INVALID, "error_word is required");
   const bool q_padded = a->q_layout == FMLM_LAYOUT_PADDED;
@@ -367,7 +378,7 @@ extern "C" int fmlm_attn_packed_fwd(const fmlm_packed_args* a, void* stream) {
   if (!a->reuse_schedule) {
     sched_kernel<<<1, kSchedThreads, 0, s>>>(a->cu_seqlens_q, has_ctx ? a->cu_seqlens_kv : a->cu_seqlens_q,
                                              ctx_index, a->batch, a->context_batch_size, has_ctx, a->causal_query_seq_attn, pr,
-                                             work, (int)cap);
+                                             work, (int)cap, a->error_word);
     if ((rc = check_launch("sched_kernel"))) return rc;
   }
 
@@ -414,9 +425,9 @@ extern "C" FMLM_API void fmlm_debug_set_trace(unsigned long long* buf) { fmlm::g
 // after start-up, and plugin hosts that hand a library only pre-allocated
 // tensors.  For them the tile schedule lives in a fixed array in device
 // memory that every GPU loading this library holds until the process exits
-// (kNoAllocScheduleInts int32 = 256 KB).  The first call on a device looks the
-// array's address up with cudaGetSymbolAddress (make that first call before
-// any stream capture); later calls reuse it.  Every call shares the array and
+// (kNoAllocScheduleInts int32 = 256 KB).  The first call in a device's
+// context looks the array's address up with cudaGetSymbolAddress (make that
+// first call before any stream capture); later calls in that context reuse it.  Every call shares the array and
 // the schedule kernel rewrites it completely on each call (nothing needs to
 // start at zero), so calls that overlap on the GPU (different streams,
 // different threads on one device) race and must be serialised by the caller.
@@ -425,22 +436,53 @@ namespace {
 constexpr int kNoAllocScheduleInts = 65536;
 static __device__ __align__(256) int g_noalloc_schedule[kNoAllocScheduleInts];
 std::mutex g_noalloc_mu;
-void* g_noalloc_ptr[64] = {};
+// The array's device address belongs to the CUDA context that looked it up,
+// so the cache is keyed by (device, context): a new primary context after
+// cudaDeviceReset, or another context made current on the same device, looks
+// the address up again.
+struct NoAllocSlot {
+  CUcontext ctx;
+  void* ptr;
+};
+NoAllocSlot g_noalloc_slot[64] = {};
+
+PFN_cuCtxGetCurrent_v4000 ctx_current_fn() {
+  static PFN_cuCtxGetCurrent_v4000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &p, 4000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuCtxGetCurrent_v4000>(p);
+  });
+  return fn;
+}
 
 int noalloc_schedule_ptr(void** out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return set_error(FMLM_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
   if (dev < 0 || dev >= 64) return set_error(FMLM_ERR_INVALID, "device index %d out of range", dev);
+  auto get_ctx = ctx_current_fn();
+  if (!get_ctx) return set_error(FMLM_ERR_CUDA, "cuCtxGetCurrent is unavailable");
+  CUcontext ctx = nullptr;
+  if (get_ctx(&ctx) != CUDA_SUCCESS) return set_error(FMLM_ERR_CUDA, "cuCtxGetCurrent failed");
   std::lock_guard<std::mutex> g(g_noalloc_mu);
-  if (!g_noalloc_ptr[dev]) {
+  NoAllocSlot& slot = g_noalloc_slot[dev];
+  if (ctx == nullptr || slot.ptr == nullptr || slot.ctx != ctx) {
+    // The lookup also makes the device's primary context current when no
+    // context is yet, so the context is read again after it.
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_noalloc_schedule);
     if (e != cudaSuccess || p == nullptr)
       return set_error(FMLM_ERR_CUDA, "cudaGetSymbolAddress(schedule scratch): %s", cudaGetErrorString(e));
-    g_noalloc_ptr[dev] = p;
+    if (get_ctx(&ctx) != CUDA_SUCCESS || ctx == nullptr)
+      return set_error(FMLM_ERR_CUDA, "no current CUDA context on device %d", dev);
+    slot.ctx = ctx;
+    slot.ptr = p;
   }
-  *out = g_noalloc_ptr[dev];
+  *out = slot.ptr;
   return FMLM_OK;
 }
 }  // namespace
@@ -448,6 +490,8 @@ int noalloc_schedule_ptr(void** out) {
 
 extern "C" int fmlm_attn_packed_fwd_noalloc(const fmlm_packed_args* a, void* stream) {
   if (!a) return set_error(FMLM_ERR_INVALID, "null args");
+  if (a->batch <= 0 || a->total_q_len < 0)
+    return set_error(FMLM_ERR_INVALID, "batch must be > 0 and total_q_len >= 0");
   const size_t have = sizeof(int) * (size_t)kNoAllocScheduleInts;
   const size_t need = fmlm_packed_workspace_bytes(a->batch, a->total_q_len, a->head_dim);
   if (need > have)

@@ -196,7 +196,10 @@ def check_device_errors(device: torch.device | None = None) -> None:
     """Synchronise and raise if any kernel on `device` reported an error.
 
     Codes: 1 = a bounded wait gave up; 2 = the dynamic shared-memory window
-    was not 1024-byte aligned (the kernel returned without touching memory).
+    was not 1024-byte aligned (the kernel returned without touching memory);
+    3 = a context_index entry was out of range (that sequence attended no
+    context); 4 = a packed sequence had more than 65536 work items (it was
+    not computed).
     """
     devs = [device] if device is not None else [torch.device("cuda", i) for i in list(_err_words)]
     for d in devs:
@@ -204,7 +207,9 @@ def check_device_errors(device: torch.device | None = None) -> None:
         v = int(w[0].item())
         if v != 0:
             w.zero_()
-            what = {1: "gave up waiting", 2: "found its shared memory misaligned"}.get(v, "failed")
+            what = {1: "gave up waiting", 2: "found its shared memory misaligned",
+                    3: "met a context_index entry out of range",
+                    4: "met a sequence too long for the tile schedule"}.get(v, "failed")
             raise FlashMLMError(f"flash_mlm kernel on {d} {what} (code {v}); results are invalid")
 
 

@@ -149,7 +149,7 @@ def flash_attn_mlm(
 
 def _packed_launch(*, q_view, k_view, v_view, q_layout, kv_layout, seq_len, total_q_len, num_heads, batch, d,
                    dtype, is_mla, prefill, causal, ctx, scale, cu_seqlens_q, out, out_rows_per_head, cache, device,
-                   context_index=None):
+                   context_index=None, owners=()):
     total_context_len = int(ctx.total_context_len)
     has_ctx = (not prefill) and total_context_len > 0
     ctx_heads = 1 if is_mla else num_heads
@@ -167,6 +167,7 @@ def _packed_launch(*, q_view, k_view, v_view, q_layout, kv_layout, seq_len, tota
     args.seq_len = seq_len
     args.total_q_len = total_q_len
     args.q, args.k, args.v = q_view, k_view, v_view
+    kc = vc = None
     if has_ctx:
         kc = ctx.k_cache.contiguous()
         vc = kc if is_mla else ctx.v_cache.contiguous()
@@ -198,15 +199,29 @@ def _packed_launch(*, q_view, k_view, v_view, q_layout, kv_layout, seq_len, tota
     args.error_word = _lib.error_word(device).data_ptr()
     with torch.cuda.device(device):
         _lib.check(L.fmlm_attn_packed_fwd(ctypes.byref(args), _lib.stream_ptr(device)), "flash_attn_mlm_compressed")
-    global last_packed_launch
-    last_packed_launch = (args, ws)
+    if _record_launches:
+        global last_packed_launch
+        keep = (tuple(owners), cu_seqlens_q, out, kc, vc, ctx.cu_seqlens_kv, context_index)
+        last_packed_launch = (_lib.PackedArgs.from_buffer_copy(args), ws, keep)
     return (ws,)
 
 
-# The argument block and workspace of the most recent packed launch.  A
-# profiler or benchmark can re-issue exactly that kernel launch through the
-# C ABI with reuse_schedule=1 (for example to time the attention kernel alone).
+# Profilers and benchmarks can ask for the argument block of the most recent
+# packed launch (record_packed_launches(True)) to re-issue exactly that kernel
+# launch through the C ABI with reuse_schedule=1, e.g. to time the attention
+# kernel alone.  The record holds the workspace and every tensor whose address
+# the argument block carries, so those pointers stay valid while it is kept.
+# Off by default: production calls keep nothing alive.
+_record_launches = False
 last_packed_launch = None
+
+
+def record_packed_launches(on: bool = True) -> None:
+    """Keep (or stop keeping, and drop) the last packed launch's arguments and buffers."""
+    global _record_launches, last_packed_launch
+    _record_launches = bool(on)
+    if not on:
+        last_packed_launch = None
 
 
 def flash_attn_mlm_compressed(
@@ -322,11 +337,13 @@ def flash_attn_mlm_compressed(
         kv_heads = 1 if is_mla else num_heads
         k_view = _lib.view_packed(k_pk, kv_heads)
         v_view = _lib.view_packed(v_pk, kv_heads)
+        k_view_src, v_view_src = k_pk, v_pk
         kv_layout = _lib.FMLM_LAYOUT_PACKED
         kv_rows = total_padded
     else:
         k_view = _lib.view_bhnd(k_main)
         v_view = _lib.view_bhnd(k_main if is_mla else v)
+        k_view_src, v_view_src = k_main, (k_main if is_mla else v)
         kv_layout = _lib.FMLM_LAYOUT_PADDED
         kv_rows = total_tokens
 
@@ -335,7 +352,7 @@ def flash_attn_mlm_compressed(
                           num_heads=num_heads, batch=b, d=d, dtype=q.dtype, is_mla=is_mla, prefill=prefill,
                           causal=causal_query_seq_attn, ctx=ctx, scale=scale, cu_seqlens_q=cu_seqlens_q, out=out,
                           out_rows_per_head=total_tokens, cache=inference_cache, device=q.device,
-                          context_index=context_index)
+                          context_index=context_index, owners=(q, k_view_src, v_view_src))
     del keep
     return out
 
@@ -439,7 +456,8 @@ def flash_attn_mlm_precompressed(
                               total_q_len=int(total_q_len), num_heads=num_heads, batch=batch, d=d, dtype=q.dtype,
                               is_mla=is_mla, prefill=prefill, causal=causal_query_seq_attn, ctx=ctx, scale=scale,
                               cu_seqlens_q=cu_seqlens_q.to(torch.int32), out=out,
-                              out_rows_per_head=int(total_q_len), cache=inference_cache, device=q.device)
+                              out_rows_per_head=int(total_q_len), cache=inference_cache, device=q.device,
+                              owners=(q, k, v))
         del keep
     if prefill and inference_cache is not None:
         inference_cache.prefill_kv_cache(layer_id, k_cache=k, v_cache=None if is_mla else v,

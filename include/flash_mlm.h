@@ -9,7 +9,10 @@
  *
  * Conventions
  *   - All pointers are device pointers unless stated otherwise.  The caller
- *     owns every buffer; the library allocates no device memory.
+ *     owns every buffer; the library allocates no device memory at run time.
+ *     One exception: fmlm_attn_packed_fwd_noalloc keeps its tile schedule in
+ *     a statically sized 256 KB __device__ array owned by the library, held on
+ *     every GPU that loads the library until exit.
  *   - `stream` is a cudaStream_t passed as void*.  Every call is asynchronous
  *     on that stream.
  *   - Return value: 0 on success, a negative FMLM_ERR_* code otherwise;
@@ -66,7 +69,9 @@ typedef struct fmlm_dense_args {
   fmlm_view4 q, k, v;         /* [B,H,N,D] */
   fmlm_view4 k_cache, v_cache;/* rows = context_len, heads = H (1 for MLA), batch = context_batch_size */
   void* out;                  /* [B,H,N,D] contiguous, dtype of q */
-  int32_t* error_word;        /* device int32; kernels set 1 if a bounded wait gave up, 2 if shared memory was misaligned */
+  int32_t* error_word;        /* device int32; kernels set 1 if a bounded wait gave up, 2 if shared memory was
+                                 misaligned (the packed path also: 3 context_index out of range, 4 a sequence
+                                 with more than 65536 work items) */
 } fmlm_dense_args;
 
 enum { FMLM_LAYOUT_PADDED = 0, FMLM_LAYOUT_PACKED = 1 };
@@ -117,8 +122,8 @@ FMLM_API int fmlm_attn_packed_fwd(const fmlm_packed_args* args, void* stream);
  * loads the library until exit).  No counterpart in the reference: it exists
  * for callers that cannot allocate device memory (capture of a CUDA graph,
  * hosts whose allocator is locked after start-up, plugin hosts that only pass
- * pre-allocated buffers).  The first call on a device looks the array up
- * (make it before any stream capture).  Problems whose schedule would exceed
+ * pre-allocated buffers).  The first call in each CUDA context of a device
+ * looks the array's address up (make it before any stream capture).  Problems whose schedule would exceed
  * the array (batch + total_q_len / 128 above about 65500) are rejected with
  * FMLM_ERR_INVALID.  All calls share the array: calls that overlap on the GPU
  * race, so serialise them. */

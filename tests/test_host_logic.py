@@ -187,6 +187,18 @@ def test_c_abi_rejects_bad_arguments_without_a_gpu():
     assert L.fmlm_attn_packed_fwd(ctypes.byref(a), None) == -2
     assert "HEAD_DIM" in L.fmlm_last_error().decode()
     assert L.fmlm_build_pack_metadata(None, 2, 4, 0, None, None, None, None, None, None) == -1
+    # negative or oversized packed sizes are rejected before any device work
+    b = _lib.PackedArgs()
+    b.dtype, b.head_dim, b.num_heads, b.batch = 1, 64, 2, 2
+    b.out, b.error_word, b.cu_seqlens_q = 16, 16, 16
+    b.q_layout = b.kv_layout = _lib.FMLM_LAYOUT_PACKED
+    b.total_q_len = -5
+    assert L.fmlm_attn_packed_fwd(ctypes.byref(b), None) == -1
+    assert "total_q_len must be >= 0" in L.fmlm_last_error().decode()
+    assert L.fmlm_attn_packed_fwd_noalloc(ctypes.byref(b), None) == -1
+    b.total_q_len = 65536 * 128
+    assert L.fmlm_attn_packed_fwd(ctypes.byref(b), None) == -1
+    assert "65536 * 128" in L.fmlm_last_error().decode()
 
 
 def test_schedule_workspace_memo_rules():

@@ -44,10 +44,14 @@ def _regular_then_args(q, k, v, cache, meta, H, D):
     from flash_mlm import _lib
     from flash_mlm.host import host as host_mod
 
-    ref = flash_mlm.flash_attn_mlm_compressed(q, k, v, num_heads=H, q_meta=meta, scale=1.0 / D ** 0.5,
-                                              inference_cache=cache, layer_id=0, block_n=64)
-    args, _ws = host_mod.last_packed_launch
-    return ref, _lib.PackedArgs.from_buffer_copy(args)
+    host_mod.record_packed_launches(True)
+    try:
+        ref = flash_mlm.flash_attn_mlm_compressed(q, k, v, num_heads=H, q_meta=meta, scale=1.0 / D ** 0.5,
+                                                  inference_cache=cache, layer_id=0, block_n=64)
+        args = _lib.PackedArgs.from_buffer_copy(host_mod.last_packed_launch[0])
+    finally:
+        host_mod.record_packed_launches(False)
+    return ref, args
 
 
 def test_noalloc_entry_matches_workspace_entry_on_two_calls_in_a_row():
@@ -75,6 +79,8 @@ def test_noalloc_entry_matches_workspace_entry_on_two_calls_in_a_row():
         err = (out.float() - ref.float()).abs().max().item()
         assert torch.isfinite(out.float()).all()
         assert err <= TOL[dtype], f"no-alloc vs workspace entry point: max abs diff {err:.3e}"
+        # Both entry points run the same kernel on the same tile schedule.
+        assert torch.equal(out, ref)
         keep.append((q, k, v, cache, meta, ref, out))
 
 
