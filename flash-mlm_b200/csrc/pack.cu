@@ -15,6 +15,10 @@
 namespace fmlm {
 namespace {
 
+// Device error word value of an append that would pass the cache capacity
+// (numbered after the attention kernel's codes 1-4).
+constexpr int kErrCacheFull = 5;
+
 constexpr int kScanThreads = 1024;
 
 __device__ int block_scan_excl(int v, int* warp_sums, int* total) {
@@ -213,6 +217,63 @@ __global__ void pad_rows_kernel(const uint8_t* __restrict__ src, long long old_l
   }
 }
 
+// Appends B sequences to a head-major context cache dst[h][cap] with spare
+// room.  base = cu_kv[eb] (the rows the cache already holds, read on the
+// device); sequence b lands at rows base + cu[b] - cu[0] ... of every head and
+// its end offset is written to cu_kv[eb + 1 + b].  Source rows come from a
+// padded [B][H][N] view (row t of batch b) or a packed [H][T] view (row
+// cu[b] + t of batch 0).  grid.y covers the K heads then the V heads.  If the
+// appended rows would pass `cap`, nothing is written and the error word is set.
+template <int V>
+__global__ void __launch_bounds__(kCopyThreads) cache_append_kernel(
+    const uint8_t* __restrict__ src_k, const uint8_t* __restrict__ src_v, long long sb, long long sh, long long sr,
+    int src_packed, int row_bytes, const int* __restrict__ cu, int B, int H, long long total_new,
+    uint8_t* __restrict__ dst_k, uint8_t* __restrict__ dst_v, long long cap, int* cu_kv, int eb, int* err) {
+  using T = typename VecT<V>::T;
+  const int nvec = row_bytes / V;
+  const bool is_v = blockIdx.y >= (unsigned)H;
+  const int h = is_v ? blockIdx.y - H : blockIdx.y;
+  const uint8_t* src_base = is_v ? src_v : src_k;
+  uint8_t* dst = is_v ? dst_v : dst_k;
+  const long long base = cu_kv[eb];
+  if (base < 0 || base + total_new > cap) {
+    if (blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && threadIdx.x == 0) atomicExch(err, kErrCacheFull);
+    return;
+  }
+  const int c0 = __ldg(cu);
+  const long long r0 = (long long)blockIdx.x * kRowsPerCta;
+  for (int b = blockIdx.z; b < B; b += gridDim.z) {
+    const int s0 = __ldg(cu + b);
+    const long long len = __ldg(cu + b + 1) - s0;
+    if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0)
+      cu_kv[eb + 1 + b] = (int)(base + (s0 - c0) + len);
+    if (r0 >= len) continue;
+    const uint8_t* src = src_packed ? src_base + h * sh + (long long)s0 * sr : src_base + b * sb + h * sh;
+    const long long dst0 = (long long)h * cap + base + (s0 - c0);
+    const int nv = (int)(len - r0 < kRowsPerCta ? len - r0 : kRowsPerCta) * nvec;
+    for (int i0 = 0; i0 < nv; i0 += kCopyThreads * kUnroll) {
+      T val[kUnroll];
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        const int i = i0 + u * kCopyThreads + threadIdx.x;
+        val[u] = T{};
+        if (i < nv) {
+          const int t = i / nvec, w = i - t * nvec;
+          val[u] = *reinterpret_cast<const T*>(src + (r0 + t) * sr + (long long)w * V);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        const int i = i0 + u * kCopyThreads + threadIdx.x;
+        if (i < nv) {
+          const int t = i / nvec, w = i - t * nvec;
+          *reinterpret_cast<T*>(dst + (dst0 + r0 + t) * row_bytes + (long long)w * V) = val[u];
+        }
+      }
+    }
+  }
+}
+
 int pick_vec(long long a) {
   for (int v = 16; v > 1; v >>= 1)
     if (a % v == 0) return v;
@@ -339,4 +400,58 @@ extern "C" int fmlm_pad_packed_rows(const void* src, int64_t old_len, int64_t ne
   }
 #undef FMLM_PAD
   return check_launch("pad_rows_kernel");
+}
+
+extern "C" int fmlm_cache_append(const fmlm_view4* k, const fmlm_view4* v, int32_t src_layout, int32_t elem_bytes,
+                                 int32_t head_dim, const int32_t* cu_seqlens, int32_t B, int64_t total_tokens,
+                                 void* k_cache, void* v_cache, int64_t capacity, int32_t* cu_seqlens_kv,
+                                 int32_t entries_before, int32_t* error_word, void* stream) {
+  if (!k || !k_cache || !cu_seqlens || !cu_seqlens_kv || !error_word)
+    return set_error(FMLM_ERR_INVALID, "null pointer argument");
+  if ((v == nullptr) != (v_cache == nullptr)) return set_error(FMLM_ERR_INVALID, "v and v_cache must be given together");
+  if (elem_bytes <= 0 || head_dim <= 0 || B < 0 || total_tokens < 0 || capacity < 0 || entries_before < 0)
+    return set_error(FMLM_ERR_INVALID, "bad cache-append sizes");
+  if (src_layout != FMLM_LAYOUT_PADDED && src_layout != FMLM_LAYOUT_PACKED)
+    return set_error(FMLM_ERR_INVALID, "src_layout must be FMLM_LAYOUT_PADDED or FMLM_LAYOUT_PACKED");
+  if (total_tokens > capacity) return set_error(FMLM_ERR_INVALID, "appended rows exceed the cache capacity");
+  if (v && (v->heads != k->heads || v->batch_stride != k->batch_stride || v->head_stride != k->head_stride ||
+            v->row_stride != k->row_stride))
+    return set_error(FMLM_ERR_INVALID, "k and v views must have the same shape and strides");
+  if (B == 0) return FMLM_OK;
+  const int H = (int)k->heads;
+  if (H <= 0 || H * (v ? 2 : 1) > 65535) return set_error(FMLM_ERR_INVALID, "bad head count");
+  if (total_tokens > 0 && (!k->data || (v && !v->data))) return set_error(FMLM_ERR_INVALID, "k/v have no data");
+  const long long row_bytes = (long long)elem_bytes * head_dim;
+  const long long sb = k->batch_stride * elem_bytes, sh = k->head_stride * elem_bytes, sr = k->row_stride * elem_bytes;
+  long long g = row_bytes;
+  for (long long a : {sb, sh, sr, (long long)reinterpret_cast<uintptr_t>(k->data),
+                      (long long)reinterpret_cast<uintptr_t>(v ? v->data : k->data),
+                      (long long)reinterpret_cast<uintptr_t>(k_cache),
+                      (long long)reinterpret_cast<uintptr_t>(v_cache ? v_cache : k_cache)})
+    g = std::__gcd(g, a == 0 ? g : a);
+  const int V = pick_vec(g);
+  // Rows per sequence are bounded by the source view (padded) or by the
+  // appended total (packed).
+  const long long max_rows = std::max<long long>(1, src_layout == FMLM_LAYOUT_PADDED ? k->rows : total_tokens);
+  const dim3 grid((unsigned)((max_rows + kRowsPerCta - 1) / kRowsPerCta), (unsigned)(H * (v ? 2 : 1)),
+                  (unsigned)std::min(B, 65535));
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  auto sk = reinterpret_cast<const uint8_t*>(k->data);
+  auto sv = reinterpret_cast<const uint8_t*>(v ? v->data : k->data);
+  auto dk = reinterpret_cast<uint8_t*>(k_cache);
+  auto dv = reinterpret_cast<uint8_t*>(v_cache ? v_cache : k_cache);
+  const int packed = src_layout == FMLM_LAYOUT_PACKED;
+#define FMLM_APPEND(VV)                                                                                           \
+  cache_append_kernel<VV><<<grid, kCopyThreads, 0, s>>>(sk, sv, sb, sh, sr, packed, (int)row_bytes, cu_seqlens, B, \
+                                                        H, total_tokens, dk, dv, capacity, cu_seqlens_kv,        \
+                                                        entries_before, error_word)
+  switch (V) {
+    case 16: FMLM_APPEND(16); break;
+    case 8: FMLM_APPEND(8); break;
+    case 4: FMLM_APPEND(4); break;
+    case 2: FMLM_APPEND(2); break;
+    default: FMLM_APPEND(1); break;
+  }
+#undef FMLM_APPEND
+  return check_launch("cache_append_kernel");
 }

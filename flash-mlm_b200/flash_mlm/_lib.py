@@ -126,6 +126,9 @@ def lib() -> ctypes.CDLL:
         L.fmlm_unpack_rows.restype = ctypes.c_int
         L.fmlm_pad_packed_rows.argtypes = [vp, i64, i64, i32, i32, i32, vp, vp]
         L.fmlm_pad_packed_rows.restype = ctypes.c_int
+        L.fmlm_cache_append.argtypes = [ctypes.POINTER(View4), ctypes.POINTER(View4), i32, i32, i32, vp, i32, i64,
+                                        vp, vp, i64, vp, i32, vp, vp]
+        L.fmlm_cache_append.restype = ctypes.c_int
         L.fmlm_last_error.argtypes = []
         L.fmlm_last_error.restype = ctypes.c_char_p
         L.fmlm_version.argtypes = []
@@ -199,7 +202,8 @@ def check_device_errors(device: torch.device | None = None) -> None:
     was not 1024-byte aligned (the kernel returned without touching memory);
     3 = a context_index entry was out of range (that sequence attended no
     context); 4 = a packed sequence had more than 65536 work items (it was
-    not computed).
+    not computed); 5 = a cache append would have passed the cache capacity
+    (nothing was written).
     """
     devs = [device] if device is not None else [torch.device("cuda", i) for i in list(_err_words)]
     for d in devs:
@@ -209,7 +213,8 @@ def check_device_errors(device: torch.device | None = None) -> None:
             w.zero_()
             what = {1: "gave up waiting", 2: "found its shared memory misaligned",
                     3: "met a context_index entry out of range",
-                    4: "met a sequence too long for the tile schedule"}.get(v, "failed")
+                    4: "met a sequence too long for the tile schedule",
+                    5: "would have overrun a context cache's capacity (nothing appended)"}.get(v, "failed")
             raise FlashMLMError(f"flash_mlm kernel on {d} {what} (code {v}); results are invalid")
 
 

@@ -28,7 +28,7 @@ import math
 import torch
 
 from flash_mlm import _lib
-from flash_mlm.host.cache import InferenceCache, PackMetadata, host_cu_seqlens
+from flash_mlm.host.cache import BATCH_MAJOR, InferenceCache, PackMetadata, host_cu_seqlens
 from flash_mlm.host.host_utils import (
     _compute_total_q_len_padded,
     _maybe_get_cache_context,
@@ -55,7 +55,7 @@ def _validate_head_dim(d: int, is_mla: bool) -> None:
 _AUTO_TUNE_PAD_BLOCK_M = 128
 
 
-def _cache_view(x: torch.Tensor | None, heads: int, rows: int, batch: int) -> _lib.View4:
+def _cache_view(x: torch.Tensor | None, heads: int, rows: int, batch: int, total: int = 0) -> _lib.View4:
     """Flat rank-2 cache [batch * heads * rows, D] as a [batch][heads][rows] view."""
     if x is None or rows == 0 or x.numel() == 0:
         return _lib.view4(None)
@@ -63,6 +63,16 @@ def _cache_view(x: torch.Tensor | None, heads: int, rows: int, batch: int) -> _l
     rs = x.stride(0)
     return _lib.view4(x, rows=rows, heads=heads, batch=batch, row_stride=rs, head_stride=rows * rs,
                       batch_stride=heads * rows * rs)
+
+
+def _heads_major_cache_view(x: torch.Tensor | None, heads: int, rows: int, batch: int, total: int) -> _lib.View4:
+    """Head-major cache [heads * total, D] whose entry c sits at rows [c * rows, (c + 1) * rows)
+    of each head, as a [batch][heads][rows] view (no copy)."""
+    if x is None or rows == 0 or x.numel() == 0:
+        return _lib.view4(None)
+    rs = x.stride(0)
+    return _lib.view4(x, rows=rows, heads=heads, batch=batch, row_stride=rs, head_stride=total * rs,
+                      batch_stride=rows * rs)
 
 
 def _workspace(device: torch.device, nbytes: int, cache: InferenceCache | None) -> torch.Tensor:
@@ -126,8 +136,10 @@ def flash_attn_mlm(
     args.scale = float(scale)
     args.q, args.k, args.v = _lib.view_bhnd(q), _lib.view_bhnd(k), _lib.view_bhnd(v)
     if has_ctx:
-        args.k_cache = _cache_view(k_cache, ctx_heads, context_len, context_batch_size)
-        args.v_cache = _cache_view(k_cache if is_mla else v_cache, ctx_heads, context_len, context_batch_size)
+        view = _cache_view if ctx.layout == BATCH_MAJOR else _heads_major_cache_view
+        total = int(ctx.total_context_len)
+        args.k_cache = view(k_cache, ctx_heads, context_len, context_batch_size, total)
+        args.v_cache = view(k_cache if is_mla else v_cache, ctx_heads, context_len, context_batch_size, total)
     args.out = out.data_ptr()
     args.error_word = _lib.error_word(q.device).data_ptr()
     if out.numel():
@@ -142,8 +154,8 @@ def flash_attn_mlm(
         else:
             k_prefill = k.contiguous().view(b * h * n, d)
             v_prefill = v.contiguous().view(b * h * n, d)
-        inference_cache.prefill_kv_cache(layer_id, k_cache=k_prefill, v_cache=v_prefill, context_batch_size=int(b),
-                                         is_mla=is_mla, num_heads=h, head_dim=d)
+        inference_cache._store_dense_prefill(layer_id, k_cache=k_prefill, v_cache=v_prefill,
+                                             context_batch_size=int(b), is_mla=is_mla, num_heads=h, head_dim=d)
     return out
 
 
@@ -375,7 +387,18 @@ def _pack_main_kv(k, v, q_meta, num_heads, is_mla, total_padded, packing, k_name
 
 
 def _store_prefill(k, v, q_meta, num_heads, is_mla, block_m, block_n, auto_tune_tiles, cache, layer_id, d):
-    """Pack this call's K/V into the layer's cache workspaces and register them (host.py:327-364)."""
+    """Pack this call's K/V into the layer's cache and register them (host.py:327-364).
+
+    A layer with a reserved cache (``InferenceCache.reserve_kv_cache``) is
+    emptied and receives the rows through one device append, with no new
+    buffer; otherwise the K/V are packed into the layer's named workspaces,
+    padded as the reference pads them."""
+    r = cache.reserved(layer_id)
+    if r is not None and r.is_mla == bool(is_mla) and r.head_dim == d and r.k.dtype == k.dtype \
+            and r.k.device == k.device and (is_mla or r.num_heads == num_heads):
+        cache.reset_kv_cache(layer_id)
+        cache.append_kv_cache(layer_id, k, None if is_mla else v, q_meta)
+        return r.k, (r.k if is_mla else r.v), r.capacity
     pad_block_m = _AUTO_TUNE_PAD_BLOCK_M if auto_tune_tiles else block_m
     total_padded = _compute_total_q_len_padded(q_meta.total_tokens, host_cu_seqlens(q_meta), pad_block_m, block_n)
     key = str(layer_id)

@@ -18,10 +18,10 @@ from typing import TYPE_CHECKING
 import torch
 
 from flash_mlm import _lib
-from flash_mlm.host.cache import InferenceCache, PackMetadata, host_cu_seqlens
+from flash_mlm.host.cache import BATCH_MAJOR, HEADS_MAJOR, InferenceCache, LayerKVEntry, PackMetadata, host_cu_seqlens
 
 if TYPE_CHECKING:
-    from flash_mlm.host.cache import LayerKVEntry, PackingCache
+    from flash_mlm.host.cache import PackingCache, _Reserved
 
 
 @dataclass
@@ -32,6 +32,9 @@ class CacheContext:
     context_len: int
     total_context_len: int
     cu_seqlens_kv: torch.Tensor | None
+    # Dense path only: "batch_major" ([C][H][context_len] rows) or "heads_major"
+    # ([H][total_context_len] rows, entry c at rows c * context_len of each head).
+    layout: str = "batch_major"
 
 
 # ---------------------------------------------------------------------------
@@ -61,13 +64,13 @@ def _run_metadata(lengths_i32: torch.Tensor, N: int, block_n: int, want_tokens: 
 
 
 def build_pack_metadata(lengths: torch.Tensor, N: int, block_n: int) -> PackMetadata:
-    """Precompute reusable indexing for variable-length packed tensors.
+    """Offsets and index maps of a padded batch whose sequence b holds
+    ``lengths[b]`` valid tokens out of ``N``.
 
-    Args:
-        lengths: (B,) int tensor with active tokens per batch entry.
-        N: padded max sequence length.
-        block_n: Q tile size used to precompute and store tile-to-batch ids
-            for packed kernel launches.
+    Runs one scan kernel and one fill kernel and reads the totals back once.
+    The result carries int32 ``cu_seqlens`` [B+1], int64 ``token_indices``
+    (flat b*N+t of every valid token), and the per-``block_n`` query tile map
+    (``batch_ids_q``, ``q_tile_starts_q``) in the reference's exact order.
     """
     if lengths.ndim != 1:
         raise ValueError("lengths must be rank-1 [B]")
@@ -122,24 +125,24 @@ def _build_query_tile_map_from_cu_seqlens(cu_seqlens_q: torch.Tensor, block_n: i
 
 
 def build_batch_ids_from_cu_seqlens(cu_seqlens_q: torch.Tensor, block_n: int):
-    """Build tile-to-batch mapping for packed query tiles."""
+    """Sequence index of every ``block_n``-row query tile of a packed batch."""
     _, batch_ids = _build_query_tile_map_from_cu_seqlens(cu_seqlens_q, block_n)
     return batch_ids
 
 
 def build_q_tile_starts_from_cu_seqlens(cu_seqlens_q: torch.Tensor, block_n: int):
-    """Build packed query start offsets for each per-batch query tile."""
+    """Packed row at which every ``block_n``-row query tile starts."""
     q_tile_starts_q, _ = _build_query_tile_map_from_cu_seqlens(cu_seqlens_q, block_n)
     return q_tile_starts_q
 
 
 def num_query_tiles_from_cu_seqlens(cu_seqlens_q: torch.Tensor, block_n: int) -> int:
-    """Return number of per-batch query tiles for a given block_n."""
+    """Count of ``block_n``-row query tiles over all sequences of ``cu_seqlens_q``."""
     return int(build_q_tile_starts_from_cu_seqlens(cu_seqlens_q, block_n).numel())
 
 
 def num_query_tiles_from_meta(meta: PackMetadata) -> int:
-    """Return number of precomputed per-batch query tiles stored in metadata."""
+    """Count of query tiles in ``meta``'s precomputed tile map."""
     return int(meta.q_tile_starts_q.numel())
 
 
@@ -224,12 +227,19 @@ def make_contiguous(*tensors: torch.Tensor | None) -> tuple[torch.Tensor | None,
 def _maybe_get_cache_context(*, inference_cache: InferenceCache | None, layer_id, batch_size: int, num_heads: int,
                              head_dim: int, is_mla: bool, context_batch_size: int | None, device: torch.device,
                              dtype: torch.dtype, compressed: bool) -> CacheContext:
-    """Resolve the context K/V for a call.
+    """Resolve the context K/V for a call (reference rules, host_utils.py:156-263).
 
     A missing or mismatching cache entry means "no context" (empty K/V).  A
-    ``context_batch_size`` of 1 over a multi-batch entry selects one shared
+    ``context_batch_size`` of 1 over a multi-entry cache selects one shared
     context covering every stored row.  The dense path needs a uniform
     context length.
+
+    Beyond the reference, the row layout of the entry is honoured: the packed
+    path reads a dense prefill's [C][H][ctx] entry through a head-major copy
+    made once (``InferenceCache.as_heads_major``), and the dense path reads a
+    head-major entry of uniform entries in place through its strides.  Where
+    the two layouts coincide (MLA, one head or one entry) the reference's
+    resolution is unchanged.
     """
     entry: LayerKVEntry | None = None
     if inference_cache is not None:
@@ -242,45 +252,90 @@ def _maybe_get_cache_context(*, inference_cache: InferenceCache | None, layer_id
     if entry is None:
         resolved = batch_size if context_batch_size is None else context_batch_size
         k_cache = torch.empty((0, head_dim), device=device, dtype=dtype)
-        v_cache = torch.empty_like(k_cache)
-        cu_kv = torch.zeros(resolved + 1, device=device, dtype=torch.int32) if compressed else None
-        return CacheContext(k_cache=k_cache, v_cache=v_cache, context_batch_size=resolved, context_len=0,
-                            total_context_len=0, cu_seqlens_kv=cu_kv)
+        return CacheContext(k_cache=k_cache, v_cache=torch.empty_like(k_cache), context_batch_size=resolved,
+                            context_len=0, total_context_len=0,
+                            cu_seqlens_kv=torch.zeros(resolved + 1, device=device, dtype=torch.int32)
+                            if compressed else None)
 
     stored = entry.context_batch_size
-    resolved = stored
-    if context_batch_size is not None:
-        if context_batch_size == 1:
-            resolved = 1
-        elif context_batch_size != stored:
-            raise ValueError(
-                f"context_batch_size ({context_batch_size}) must match cached entry context_batch_size ({stored})"
-            )
+    if context_batch_size is None or context_batch_size == stored:
+        resolved = stored
+    elif context_batch_size == 1:
+        resolved = 1
+    else:
+        raise ValueError(
+            f"context_batch_size ({context_batch_size}) must match cached entry context_batch_size ({stored})"
+        )
     if resolved < 1:
         raise ValueError("context_batch_size must be >= 1")
 
-    total = int(entry.total_context_len)
-    context_len = 0
+    # Layout matters only with several heads and several entries.
+    layouts_differ = not is_mla and num_heads > 1 and stored > 1
     if compressed:
-        cu_kv = entry.cu_seqlens_kv
-        if cu_kv is None:
-            if total % stored != 0:
-                raise ValueError("compressed path requires cu_seqlens_kv or uniform per-batch context lengths")
-            context_len = total // stored
-            cu_kv = torch.arange(stored + 1, device=device, dtype=torch.int32) * int(context_len)
-        if resolved == 1 and stored != 1:
-            cu_kv = torch.tensor([0, total], device=device, dtype=torch.int32)
-    else:
-        cu_kv = None
-        if total % resolved != 0:
-            raise ValueError("dense flash_attn_mlm requires uniform per-batch context lengths")
-        context_len = total // resolved
-        expected = total if is_mla else num_heads * total
-        if entry.k_cache.shape[0] != expected or (not is_mla and entry.v_cache.shape[0] != expected):
-            raise ValueError("cached dense k/v rows mismatch expected layout for is_mla/num_heads")
+        return _packed_context(inference_cache, entry, resolved, layouts_differ, device)
+    return _dense_context(inference_cache, entry, resolved, layouts_differ, is_mla, num_heads)
 
+
+def _packed_context(cache, entry, resolved, layouts_differ, device) -> CacheContext:
+    if layouts_differ and entry.layout == BATCH_MAJOR:
+        entry = cache.as_heads_major(entry)
+    total = int(entry.total_context_len)
+    stored = entry.context_batch_size
+    context_len = 0
+    cu_kv = entry.cu_seqlens_kv
+    if cu_kv is None:
+        if total % stored != 0:
+            raise ValueError("compressed path requires cu_seqlens_kv or uniform per-batch context lengths")
+        context_len = total // stored
+        cu_kv = torch.arange(stored + 1, device=device, dtype=torch.int32) * int(context_len)
+    if resolved == 1 and stored != 1:
+        cu_kv = torch.tensor([0, int(entry.used_context_len)], device=device, dtype=torch.int32)
     return CacheContext(k_cache=entry.k_cache, v_cache=entry.v_cache, context_batch_size=resolved,
-                        context_len=context_len, total_context_len=total, cu_seqlens_kv=cu_kv)
+                        context_len=context_len, total_context_len=total, cu_seqlens_kv=cu_kv,
+                        layout=HEADS_MAJOR)
+
+
+def _entry_offsets(entry: LayerKVEntry) -> list[int]:
+    """Host copy of an entry's context offsets (one device read, memoised on the entry)."""
+    if entry.cu_host is None:
+        if entry.cu_seqlens_kv is None:
+            step = int(entry.total_context_len) // entry.context_batch_size
+            entry.cu_host = [c * step for c in range(entry.context_batch_size + 1)]
+        else:
+            entry.cu_host = [int(x) for x in entry.cu_seqlens_kv.to("cpu").tolist()]
+    return entry.cu_host
+
+
+def _dense_context(cache, entry, resolved, layouts_differ, is_mla, num_heads) -> CacheContext:
+    stored = entry.context_batch_size
+    layout = BATCH_MAJOR
+    if layouts_differ and entry.layout == BATCH_MAJOR and resolved == 1:
+        # one shared context over every stored row of a head: read it head-major
+        entry = cache.as_heads_major(entry)
+        layout = HEADS_MAJOR
+    elif layouts_differ and entry.layout == HEADS_MAJOR and resolved == stored:
+        # per-entry context from a head-major cache: uniform entries, read in place
+        cu = _entry_offsets(entry)[: stored + 1]
+        step = cu[1] - cu[0]
+        if any(cu[c] != cu[0] + c * step for c in range(stored + 1)) or cu[0] != 0:
+            raise ValueError("dense flash_attn_mlm requires uniform per-batch context lengths")
+        return CacheContext(k_cache=entry.k_cache, v_cache=entry.v_cache, context_batch_size=resolved,
+                            context_len=step, total_context_len=int(entry.total_context_len), cu_seqlens_kv=None,
+                            layout=HEADS_MAJOR)
+    elif entry.layout == HEADS_MAJOR and resolved == 1:
+        layout = HEADS_MAJOR
+    total = int(entry.total_context_len)
+    if resolved == 1 and stored != 1:
+        total = int(entry.used_context_len)
+    if total % resolved != 0:
+        raise ValueError("dense flash_attn_mlm requires uniform per-batch context lengths")
+    context_len = total // resolved
+    expected = int(entry.total_context_len) * (1 if is_mla else num_heads)
+    if entry.k_cache.shape[0] != expected or (not is_mla and entry.v_cache.shape[0] != expected):
+        raise ValueError("cached dense k/v rows mismatch expected layout for is_mla/num_heads")
+    return CacheContext(k_cache=entry.k_cache, v_cache=entry.v_cache, context_batch_size=resolved,
+                        context_len=context_len, total_context_len=int(entry.total_context_len),
+                        cu_seqlens_kv=None, layout=layout)
 
 
 # ---------------------------------------------------------------------------
@@ -436,3 +491,59 @@ def unpack_from_kernel(packed: torch.Tensor, meta: PackMetadata, H: int):
                                             out.data_ptr(), _lib.stream_ptr(packed.device)),
                 "unpack_from_kernel")
     return out
+
+
+# ---------------------------------------------------------------------------
+# context-cache appends (no reference counterpart: the reference stores a new
+# packed buffer per prefill, src/flash_mlm/host/host.py:327-364)
+
+
+def _append_launch(k_view, v_view, src_layout, elem_bytes, d, cu, B, total, k_dst, v_dst, capacity, cu_kv,
+                   entries_before, device):
+    err = _lib.error_word(device)
+    with torch.cuda.device(device):
+        _lib.check(
+            _lib.lib().fmlm_cache_append(ctypes.byref(k_view), ctypes.byref(v_view) if v_view is not None else None,
+                                         src_layout, elem_bytes, d, cu.data_ptr(), B, total, k_dst.data_ptr(),
+                                         v_dst.data_ptr() if v_dst is not None else None, capacity,
+                                         cu_kv.data_ptr(), entries_before, err.data_ptr(),
+                                         _lib.stream_ptr(device)),
+            "fmlm_cache_append")
+
+
+def append_rows_into_cache(k: torch.Tensor, v: torch.Tensor | None, meta: PackMetadata, r: "_Reserved") -> None:
+    """Append the valid rows of padded k / v [B, H, N, D] to reserved cache ``r`` (one launch)."""
+    _lib.require_cuda(k, v, meta.cu_seqlens, what="append_kv_cache")
+    if meta.B != k.shape[0] or meta.N != k.shape[2]:
+        raise ValueError("k shape mismatch with PackMetadata")
+    if k.stride(-1) != 1 or (v is not None and v.stride() != k.stride()):
+        k = k.contiguous()
+        v = None if v is None else v.contiguous()
+    if meta.B == 0:
+        return
+    _append_launch(_lib.view_bhnd(k), None if v is None else _lib.view_bhnd(v), _lib.FMLM_LAYOUT_PADDED,
+                   k.element_size(), k.shape[3], meta.cu_seqlens, meta.B, meta.total_tokens, r.k, r.v, r.capacity,
+                   r.cu, r.entries, k.device)
+
+
+def convert_batch_major_entry(entry: LayerKVEntry) -> LayerKVEntry:
+    """Head-major copy of a dense-prefill entry: [C][H][ctx] rows -> [H][C * ctx] rows
+    with cu_seqlens_kv = c * ctx (one ``fmlm_cache_append`` launch)."""
+    C, H, d = entry.context_batch_size, entry.num_heads, entry.head_dim
+    ctx = int(entry.total_context_len) // C
+    dev = entry.device
+    cu_src = torch.arange(C + 1, dtype=torch.int32, device=dev) * ctx
+    cu_kv = torch.zeros(C + 1, dtype=torch.int32, device=dev)
+    k_dst = torch.empty((H * C * ctx, d), dtype=entry.dtype, device=dev)
+    v_dst = torch.empty_like(k_dst)
+
+    def view(x):
+        return _lib.view4(x, rows=ctx, heads=H, batch=C, row_stride=d, head_stride=ctx * d,
+                          batch_stride=H * ctx * d)
+
+    if C * ctx > 0:
+        _append_launch(view(entry.k_cache), view(entry.v_cache), _lib.FMLM_LAYOUT_PADDED, k_dst.element_size(), d,
+                       cu_src, C, C * ctx, k_dst, v_dst, C * ctx, cu_kv, 0, dev)
+    return LayerKVEntry(k_cache=k_dst, v_cache=v_dst, total_context_len=C * ctx, cu_seqlens_kv=cu_kv,
+                        context_batch_size=C, is_mla=False, num_heads=H, head_dim=d, dtype=entry.dtype,
+                        device=dev, layout=HEADS_MAJOR, cu_host=[c * ctx for c in range(C + 1)])

@@ -4,11 +4,14 @@ The attention has no exchange step: every (sequence, head) pair is
 independent.  A job is therefore split across ranks with no collective on the
 data path:
 
-* by heads when the head count divides evenly: rank r owns heads
-  [r*H/W, (r+1)*H/W) of every sequence and keeps the matching contiguous row
-  block [h0*Tctx, h1*Tctx) of the head-major KV cache (its KV shard);
-* otherwise by sequences, balanced by attention cost (query rows x key rows,
-  longest first); MLA (a single latent KV head) always shards by sequences.
+* by heads: rank r owns a contiguous block of heads [h0, h1) of every
+  sequence (blocks as even as the head count allows) and keeps the matching
+  contiguous row block [h0*Tctx, h1*Tctx) of the head-major KV cache (its KV
+  shard); a job with causal_query_seq_attn (every sequence also reads the keys
+  of all earlier ones) is always split this way;
+* by sequences, balanced by attention cost (query rows x key rows, longest
+  first), when asked or when the heads do not divide evenly; MLA (a single
+  latent KV head) always shards by sequences.
 
 ``gather_packed_output`` reassembles the packed output on every rank with one
 all-gather (NCCL over NVLink on GPUs, gloo on CPU) when a caller needs the full
@@ -41,14 +44,36 @@ def _costs(lengths, context_lengths, causal):
 
 
 def plan_shards(lengths: list[int], num_heads: int, world_size: int, *, context_lengths: list[int] | None = None,
-                causal: bool = False, is_mla: bool = False) -> list[ShardPlan]:
-    """Deterministic plan for every rank (each rank can compute it locally)."""
+                causal: bool = False, is_mla: bool = False, mode: str = "auto") -> list[ShardPlan]:
+    """Deterministic plan for every rank (each rank can compute it locally).
+
+    ``mode``: "heads" splits the heads into contiguous blocks as evenly as
+    possible (block sizes differ by at most one); "batch" splits the
+    sequences, balanced by cost (longest processing time first); "auto" uses
+    heads when they divide evenly and batch otherwise.  MLA (one latent KV
+    head shared by all query heads) is always split by sequences.  With
+    ``causal_query_seq_attn`` a sequence also reads the keys of every earlier
+    sequence, so a causal job is always split by heads.
+    """
     if world_size < 1:
         raise ValueError("world_size must be >= 1")
+    if mode not in ("auto", "heads", "batch"):
+        raise ValueError("mode must be 'auto', 'heads' or 'batch'")
     B = len(lengths)
-    if not is_mla and num_heads % world_size == 0:
-        per = num_heads // world_size
-        return [ShardPlan(r, world_size, "heads", (r * per, (r + 1) * per), list(range(B))) for r in range(world_size)]
+    if is_mla:
+        if causal and world_size > 1:
+            raise ValueError("MLA with causal_query_seq_attn cannot be split across ranks")
+        mode = "batch"
+    elif causal:
+        mode = "heads"
+    elif mode == "auto":
+        mode = "heads" if num_heads % world_size == 0 else "batch"
+    if mode == "heads":
+        if num_heads < world_size:
+            raise ValueError("a heads split needs at least one head per rank")
+        bounds = [r * num_heads // world_size for r in range(world_size + 1)]
+        return [ShardPlan(r, world_size, "heads", (bounds[r], bounds[r + 1]), list(range(B)))
+                for r in range(world_size)]
     costs = _costs(lengths, context_lengths, causal)
     order = sorted(range(B), key=lambda b: (-costs[b], b))
     load = [0] * world_size

@@ -160,6 +160,28 @@ FMLM_API int fmlm_unpack_rows(const void* packed, int64_t total_tokens, int32_t 
                      int32_t elem_bytes, const int32_t* cu_seqlens, int32_t B, int32_t N, void* out,
                      void* stream);
 
+/* Append B sequences of K (and V) rows to a head-major context cache with spare
+ * capacity: k_cache / v_cache are [H][capacity][D] (MLA: H = 1, v = v_cache =
+ * NULL).  The cache already holds cu_seqlens_kv[entries_before] rows per head
+ * (read on the device); sequence b (length cu_seqlens[b+1] - cu_seqlens[b]) is
+ * written at row cu_seqlens_kv[entries_before] + cu_seqlens[b] - cu_seqlens[0]
+ * of every head, and cu_seqlens_kv[entries_before + 1 + b] receives its end
+ * offset, so cu_seqlens_kv[0 .. entries_before + B] describes every entry
+ * without a host round trip.  src_layout FMLM_LAYOUT_PADDED: k / v are
+ * [B][H][N][D] views (row t of batch b); FMLM_LAYOUT_PACKED: [H][T][D] views
+ * (row cu_seqlens[b] + t, batch 1).  total_tokens = cu_seqlens[B] - cu_seqlens[0].
+ * If the appended rows would pass `capacity`, nothing is written and
+ * *error_word is set to 5.
+ * Replaces the prefill store of flash_attn_mlm_compressed / precompressed
+ * (src/flash_mlm/host/host.py:327-364, :775-787), which packs this call's K/V into a
+ * new per-layer buffer, with an append into a preallocated one; with a padded
+ * [B][H][ctx] source and uniform cu_seqlens it also converts the dense
+ * prefill layout (src/flash_mlm/host/host.py:206-223) to the packed one. */
+FMLM_API int fmlm_cache_append(const fmlm_view4* k, const fmlm_view4* v, int32_t src_layout, int32_t elem_bytes,
+                               int32_t head_dim, const int32_t* cu_seqlens, int32_t B, int64_t total_tokens,
+                               void* k_cache, void* v_cache, int64_t capacity, int32_t* cu_seqlens_kv,
+                               int32_t entries_before, int32_t* error_word, void* stream);
+
 /* Copy packed [H * old_len, D] into [H * new_len, D] with zero rows appended per head.
  * Replaces the pad step of pad_packed_main_tensors_for_mlm_compressed
  * (src/flash_mlm/host/host_utils.py:494-584). */

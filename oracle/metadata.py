@@ -85,3 +85,22 @@ def pad_packed_rows(x: np.ndarray, heads: int, old_len: int, new_len: int) -> np
     out = np.zeros((heads, new_len, D), dtype=x.dtype)
     out[:, :old_len, :] = x.reshape(heads, old_len, D)
     return out.reshape(heads * new_len, D)
+
+
+def cache_append(cache: np.ndarray, cu_kv: list, x: np.ndarray, cu_src) -> tuple[np.ndarray, list]:
+    """Append the valid rows of padded x [B, H, N, D] to a head-major cache
+    [H * capacity, D] holding entries cu_kv (host list); returns the new cache
+    and offsets.  Restates what the reference's prefill stores for each
+    sequence (packed rows per head, src/flash_mlm/host/host.py:327-364) written
+    after the rows already held instead of into a new buffer."""
+    B, H, _, D = x.shape
+    cap = cache.shape[0] // H
+    out = cache.copy().reshape(H, cap, D)
+    cu = [int(c) for c in cu_src]
+    base = int(cu_kv[-1])
+    new_cu = list(cu_kv)
+    for b in range(B):
+        L = cu[b + 1] - cu[b]
+        out[:, base + cu[b] - cu[0]: base + cu[b] - cu[0] + L] = x[b, :, :L]
+        new_cu.append(base + cu[b + 1] - cu[0])
+    return out.reshape(H * cap, D), new_cu

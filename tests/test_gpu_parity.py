@@ -34,26 +34,31 @@ def half_ulp(ref: torch.Tensor, dtype) -> torch.Tensor:
     return 0.5 * torch.pow(2.0, e - mant)
 
 
-def assert_close_tol(got: torch.Tensor, ref, dtype, what="", v_scale=1.0):
-    """Error against fp32 math, beyond the output format's own rounding, must be <= TOL * v_scale.
+# Raw max-abs-error bound of the north star: 2e-3 (f16), 8e-3 (bf16) against
+# fp32 math on the same rounded inputs.  One exception, bf16 only: where
+# |o| >= 2 the output format itself cannot get nearer than 7.8e-3 (half its
+# spacing in [2, 4)), so there the bound is TOL plus that half-spacing.  Every
+# call reports how many positions the exception covered (`last_tol_report`).
+last_tol_report: dict = {}
 
-    The kernel's output is f16/bf16, so it cannot be nearer to the fp32 value
-    than half an ulp of that format (bf16: 7.8e-3 for |o| in [2, 4)); the
-    tolerance bounds the error on top of that unavoidable rounding.  P is
-    rounded to the input format before P V (as in the reference kernel), so
-    that part of the error grows with |V|: tests whose V is far above unit
-    scale pass max(1, max |V|) as v_scale.
-    """
+
+def assert_close_tol(got: torch.Tensor, ref, dtype, what=""):
     ref_t = torch.as_tensor(ref, dtype=torch.float32)
     g = got.detach().float().cpu()
     assert torch.isfinite(g).all(), f"{what}: non-finite output"
     if not g.numel():
-        return
+        return 0.0
     raw = (g - ref_t).abs()
-    excess = (raw - half_ulp(ref_t, dtype)).clamp_min(0).max().item()
-    tol = TOL[dtype] * max(1.0, float(v_scale))
-    assert excess <= tol, (f"{what}: error beyond output rounding {excess:.3e} > {tol:.1e} "
-                           f"(raw max abs err {raw.max().item():.3e})")
+    bound = torch.full_like(raw, TOL[dtype])
+    wide = torch.zeros_like(raw, dtype=torch.bool)
+    if dtype == torch.bfloat16:
+        wide = ref_t.abs() >= 2.0
+        bound = torch.where(wide, bound + half_ulp(ref_t, dtype), bound)
+    last_tol_report.update(what=what, max_abs_err=raw.max().item(), n=raw.numel(), n_wide=int(wide.sum()))
+    bad = raw > bound
+    assert not bad.any(), (f"{what}: max abs err {raw.max().item():.3e} > {TOL[dtype]:.0e} at "
+                           f"{int(bad.sum())} of {raw.numel()} positions")
+    return raw.max().item()
 
 
 def no_device_errors():
@@ -458,17 +463,16 @@ def test_large_logits_rescale_path(D):
     B, H, N = 2, 2, 640
     dt = torch.float16
     q = _rand((B, H, N, D), dt, g, 3.0)
-    k = _rand((B, H, N, D), dt, g, 3.0)
-    # increasing key norms along the sequence make later blocks raise the max
-    ramp = torch.linspace(0.2, 2.0, N).view(1, 1, N, 1)
-    k = (k.float() * ramp).to(dt)
+    # key norms grow along the sequence (later blocks raise the row max many
+    # times over); keys are clamped to |k| <= 1.5 so that, with MLA where V is
+    # K, |o| < 2 and the raw f16 bound applies unchanged
+    ramp = torch.linspace(0.1, 1.0, N).view(1, 1, N, 1)
+    k = (torch.randn((B, H, N, D), generator=g) * ramp).clamp(-1.5, 1.5).to(dt)
     v = k if is_mla else _rand((B, H, N, D), dt, g)
     scale = 4.0 / math.sqrt(D)
     out = fm().flash_attn_mlm(q.to(DEV), k.to(DEV), v.to(DEV), scale=scale, is_mla=is_mla)
     ref = oracle.attention_dense(q.float().numpy(), k.float().numpy(), v.float().numpy(), scale, is_mla=is_mla)
-    # With MLA, V is the ramped K (|V| up to ~18 here): the bound scales with |V|.
-    v_scale = float(v.float().abs().max()) if is_mla else 1.0
-    assert_close_tol(out, ref, dt, f"rescale D={D}", v_scale=v_scale)
+    assert_close_tol(out, ref, dt, f"rescale D={D}")
     no_device_errors()
 
 
@@ -664,3 +668,52 @@ def test_bounded_wait_gives_up_and_context_stays_usable():
     out = fm().flash_attn_mlm(q, q, q, scale=0.125)
     ref = torch.softmax((q.float() @ q.float().transpose(-1, -2)) * 0.125, -1) @ q.float()
     assert (out.float() - ref).abs().max().item() < 2e-3
+
+
+# ----------------------------------------------------------------- precompressed entry against the oracle
+
+
+@pytest.mark.parametrize("is_mla,causal,dt", [(False, False, torch.float16), (False, True, torch.bfloat16),
+                                              (True, False, torch.bfloat16), (True, True, torch.float16)])
+def test_precompressed_vs_oracle(is_mla, causal, dt):
+    """flash_attn_mlm_precompressed on packed inputs with a per-sequence context, against the fp32 oracle."""
+    from flash_mlm.host.host_utils import pack_for_kernel
+
+    g = torch.Generator().manual_seed(600 + 2 * is_mla + causal)
+    B, H, N, D = 4, 3, 150, (512 if is_mla and not causal else 64)
+    lengths = torch.tensor([150, 1, 77, 129], dtype=torch.int32)
+    q = _rand((B, H, N, D), dt, g, 0.5 if is_mla else 1.0)
+    k = _rand((B, H, N, D), dt, g, 0.5 if is_mla else 1.0)
+    v = _rand((B, H, N, D), dt, g)
+    ctx = torch.tensor([64, 0, 200, 31], dtype=torch.int32)
+    cu_kv = torch.cat([torch.zeros(1, dtype=torch.int32), ctx.cumsum(0).to(torch.int32)])
+    tcl = int(cu_kv[-1])
+    rows = tcl if is_mla else H * tcl
+    kc = _rand((rows, D), dt, g, 0.5 if is_mla else 1.0)
+    vc = kc if is_mla else _rand((rows, D), dt, g)
+    cache = fm().InferenceCache()
+    cache.prefill_kv_cache(0, k_cache=kc.to(DEV), v_cache=None if is_mla else vc.to(DEV), total_context_len=tcl,
+                           cu_seqlens_kv=cu_kv.to(DEV), context_batch_size=B, is_mla=is_mla, num_heads=H,
+                           head_dim=D)
+    meta = fm().build_pack_metadata(lengths.to(DEV), N, 32)
+    qp = pack_for_kernel(q.to(DEV), meta, flatten_for_kernel=True)
+    if is_mla:
+        kp = pack_for_kernel(k[:, :1].to(DEV), meta, flatten_for_kernel=True)
+        vp = kp
+    else:
+        kp = pack_for_kernel(k.to(DEV), meta, flatten_for_kernel=True)
+        vp = pack_for_kernel(v.to(DEV), meta, flatten_for_kernel=True)
+    T = meta.total_tokens
+    scale = D ** -0.5
+    out = fm().flash_attn_mlm_precompressed(qp, kp, vp, num_heads=H, total_q_len=T, cu_seqlens_q=meta.cu_seqlens,
+                                            batch_ids_q=meta.batch_ids_q, q_tile_starts_q=meta.q_tile_starts_q,
+                                            scale=scale, inference_cache=cache, layer_id=0, is_mla=is_mla,
+                                            block_m=32, block_n=32, causal_query_seq_attn=causal)
+    kk = k[:, :1].expand(B, H, N, D) if is_mla else k
+    ref = oracle.attention_packed(q.float().numpy(), kk.float().numpy(), v.float().numpy(),
+                                  meta.cu_seqlens.cpu().numpy(), scale, k_cache=kc.float().numpy(),
+                                  v_cache=vc.float().numpy(), cu_kv=cu_kv.numpy(), context_batch_size=B,
+                                  total_context_len=tcl, is_mla=is_mla, causal_query_seq_attn=causal)
+    assert out.shape == (H * T, D)
+    assert_close_tol(out, ref, dt, f"precompressed mla={is_mla} causal={causal}")
+    no_device_errors()

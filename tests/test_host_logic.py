@@ -105,6 +105,68 @@ def test_cache_context_uniform_synthesis_and_dense_rule():
                                    is_mla=False, context_batch_size=None, device=CPU, dtype=torch.float32,
                                    compressed=False)
     assert ctx.context_len == 3
+    # a head-major entry serves the dense path in place: [H][3 * 3] rows, entry c at rows 3c of each head
+    assert ctx.layout == "heads_major" and ctx.k_cache is k and ctx.total_context_len == 9
+
+
+def test_cache_layouts_seen_by_each_path():
+    """Dense prefill entries are batch-major; head-major entries with uneven entries cannot serve the dense path."""
+    cache = InferenceCache()
+    k = torch.zeros(3 * 2 * 4, 8)
+    cache._store_dense_prefill(1, k_cache=k, v_cache=k.clone(), context_batch_size=3, is_mla=False, num_heads=2,
+                               head_dim=8)
+    e = cache.get_kv_cache(1, is_mla=False, num_heads=2, head_dim=8, dtype=torch.float32, device=CPU)
+    assert e.layout == "batch_major" and e.total_context_len == 12
+    ctx = _maybe_get_cache_context(inference_cache=cache, layer_id=1, batch_size=3, num_heads=2, head_dim=8,
+                                   is_mla=False, context_batch_size=None, device=CPU, dtype=torch.float32,
+                                   compressed=False)
+    assert ctx.layout == "batch_major" and ctx.context_len == 4
+    # MLA and single-head caches have one layout: no conversion is ever needed
+    cache._store_dense_prefill(2, k_cache=torch.zeros(6, 8), v_cache=None, context_batch_size=3, is_mla=True,
+                               num_heads=4, head_dim=8)
+    assert cache.get_kv_cache(2, is_mla=True, num_heads=4, head_dim=8, dtype=torch.float32,
+                              device=CPU).layout == "heads_major"
+    # uneven head-major entries: the dense path refuses them (reference message)
+    cache.prefill_kv_cache(3, k_cache=torch.zeros(2 * 7, 8), v_cache=torch.zeros(2 * 7, 8), total_context_len=7,
+                           cu_seqlens_kv=torch.tensor([0, 2, 7], dtype=torch.int32), context_batch_size=2,
+                           is_mla=False, num_heads=2, head_dim=8)
+    with pytest.raises(ValueError, match="requires uniform per-batch context lengths"):
+        _maybe_get_cache_context(inference_cache=cache, layer_id=3, batch_size=2, num_heads=2, head_dim=8,
+                                 is_mla=False, context_batch_size=None, device=CPU, dtype=torch.float32,
+                                 compressed=False)
+
+
+def test_reserved_cache_bookkeeping_and_limits():
+    from flash_mlm.host.cache import PackMetadata
+
+    cache = InferenceCache()
+    cache.reserve_kv_cache(0, capacity=10, max_entries=2, is_mla=False, num_heads=2, head_dim=8,
+                           dtype=torch.float16, device=CPU)
+    r = cache.reserved(0)
+    assert r.k.shape == (20, 8) and r.v.shape == (20, 8) and r.cu.tolist() == [0, 0, 0]
+    with pytest.raises(ValueError, match="No cached KV context"):
+        cache.get_kv_cache(0, is_mla=False, num_heads=2, head_dim=8, dtype=torch.float16, device=CPU)
+
+    def meta(lengths, N):
+        cu = [0]
+        for x in lengths:
+            cu.append(cu[-1] + x)
+        t = torch.tensor(cu, dtype=torch.int32)
+        m = PackMetadata(B=len(lengths), N=N, lengths=torch.tensor(lengths, dtype=torch.int32), cu_seqlens=t,
+                         token_indices=torch.zeros(0, dtype=torch.int64), total_tokens=cu[-1], batch_ids_block_n=4,
+                         batch_ids_q=torch.zeros(0, dtype=torch.int32), q_tile_starts_q=torch.zeros(0, dtype=torch.int32))
+        m._cu_host = cu
+        return m
+
+    k = torch.zeros(3, 2, 6, 8, dtype=torch.float16)
+    with pytest.raises(ValueError, match="exceeds max_entries=2"):
+        cache.append_kv_cache(0, k, k, meta([1, 1, 1], 6))
+    with pytest.raises(ValueError, match="exceeds capacity=10"):
+        cache.append_kv_cache(0, k[:2], k[:2], meta([6, 5], 6))
+    with pytest.raises(ValueError, match="No reserved KV cache"):
+        cache.append_kv_cache(9, k, k, meta([1, 1, 1], 6))
+    cache.clear_layer(0)
+    assert cache.reserved(0) is None
 
 
 def test_inference_cache_validation_messages():
@@ -223,7 +285,7 @@ def test_schedule_workspace_memo_rules():
     keep = [torch.zeros(2, dtype=torch.int32) for _ in range(PackingCache._MAX_SCHEDULES + 2)]
     for t in keep:
         pc.schedule_workspace((t,), ("k",), 64, dev)
-    assert len(pc._schedules) == PackingCache._MAX_SCHEDULES
+    assert pc._store.size("schedule") == PackingCache._MAX_SCHEDULES
     assert not pc.schedule_workspace((keep[0],), ("k",), 64, dev)[1]
     pc.clear()
-    assert pc._schedules == []
+    assert pc._store.size("schedule") == 0

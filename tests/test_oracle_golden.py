@@ -93,3 +93,34 @@ def test_oracle_attention_matches_reference_fp32(name):
     params, t = attention_case(name)
     got = run_oracle_case(params, t)
     np.testing.assert_allclose(got, t["out"].numpy(), atol=2e-5, rtol=0)
+
+
+def run_torch_ref_case(params, t):
+    """The torch restatement of the reference's CPU path on a golden case."""
+    import torch
+
+    from oracle import torch_ref
+
+    q, k, v = (t[x].float() for x in ("q", "k", "v"))
+    if params["kind"] == "dense":
+        return torch_ref.dense_attention_with_cache(
+            q, k, v, params["scale"], k_cache=t["k_cache"].float() if "k_cache" in t else None,
+            v_cache=t["v_cache"].float() if "v_cache" in t else None, context_len=params["context_len"],
+            context_batch_size=params["context_batch_size"], is_mla=params["is_mla"]).numpy()
+    lengths = t["lengths"].numpy()
+    B, H, N, D = q.shape
+    cu = np.concatenate([[0], np.cumsum(lengths)]).astype(np.int64)
+    kw = {}
+    if params["ctx"] != "none":
+        kw = dict(k_cache=t["k_cache"].float(), v_cache=t["v_cache"].float(), cu_kv=t["cu_kv"].tolist(),
+                  context_batch_size=params["context_batch_size"], total_context_len=params["total_context_len"])
+    packed = torch_ref.varlen_attention_with_cache(q, k, v, cu, params["scale"], is_mla=params["is_mla"],
+                                                   causal_query_seq_attn=params["causal"], **kw)
+    return oracle.unpack_rows(packed.numpy(), cu, H, N)
+
+
+@pytest.mark.parametrize("name", [c["name"] for c in attention_manifest()])
+def test_torch_cpu_path_matches_reference_fp32(name):
+    params, t = attention_case(name)
+    got = run_torch_ref_case(params, t)
+    np.testing.assert_allclose(got, t["out"].numpy(), atol=2e-5, rtol=0)
