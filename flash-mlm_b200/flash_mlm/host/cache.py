@@ -170,11 +170,15 @@ class PackingCache:
 # Row layouts of a cached entry (non-MLA; an MLA cache has one latent head, so
 # both layouts coincide):
 #   "heads_major": [H][total_context_len] rows, entries at cu_seqlens_kv offsets
-#                  (what the packed path and prefill_kv_cache store).
+#                  (what the packed path's prefill and append store).
 #   "batch_major": [C][H][context_len] rows, uniform per-entry length
 #                  (what the dense path's prefill stores).
+#   "as_given":    buffers handed to prefill_kv_cache; as in the reference, the
+#                  packed path reads them head-major and the dense path
+#                  batch-major, with no conversion.
 HEADS_MAJOR = "heads_major"
 BATCH_MAJOR = "batch_major"
+AS_GIVEN = "as_given"
 
 
 @dataclass
@@ -190,7 +194,7 @@ class LayerKVEntry:
     dtype: torch.dtype
     device: torch.device
     # --- beyond the reference ---
-    layout: str = HEADS_MAJOR
+    layout: str = AS_GIVEN
     # Rows per head that hold context (a reserved cache has spare rows after them).
     used_context_len: int | None = None
     # Host copy of cu_seqlens_kv when the writer knew it (saves a device read).
@@ -297,7 +301,7 @@ class InferenceCache:
         """
         self._store_entry(layer_id, k_cache=k_cache, v_cache=v_cache, total_context_len=total_context_len,
                           cu_seqlens_kv=cu_seqlens_kv, context_batch_size=context_batch_size, is_mla=is_mla,
-                          num_heads=num_heads, head_dim=head_dim, layout=HEADS_MAJOR)
+                          num_heads=num_heads, head_dim=head_dim, layout=AS_GIVEN)
 
     def get_kv_cache(self, layer_id: int | str, *, is_mla: bool, num_heads: int, head_dim: int,
                      dtype: torch.dtype, device: torch.device) -> LayerKVEntry:
@@ -353,9 +357,13 @@ class InferenceCache:
             cu_seqlens_kv=None if cu_seqlens_kv is None else cu_seqlens_kv.contiguous(),
             context_batch_size=int(context_batch_size), is_mla=bool(is_mla), num_heads=int(num_heads),
             head_dim=int(head_dim), dtype=k_cache.dtype, device=k_cache.device,
-            layout=HEADS_MAJOR if is_mla else layout, used_context_len=used_context_len, cu_host=cu_host)
+            layout=layout, used_context_len=used_context_len, cu_host=cu_host)
         self._entries[str(layer_id)] = entry
         return entry
+
+    def _store_packed_prefill(self, layer_id, **kw) -> None:
+        """Entry written by a packed launcher's prefill: head-major rows (host.py:351-364)."""
+        self._store_entry(layer_id, layout=HEADS_MAJOR, **kw)
 
     def _store_dense_prefill(self, layer_id, *, k_cache, v_cache, context_batch_size, is_mla, num_heads,
                              head_dim) -> None:
@@ -435,7 +443,7 @@ class InferenceCache:
         itself, or (for a batch-major entry of a dense prefill with several
         entries and heads) a converted copy made once on the device by
         ``fmlm_cache_append`` and kept on the entry."""
-        if entry.layout == HEADS_MAJOR or entry.context_batch_size == 1 or entry.num_heads == 1:
+        if entry.layout != BATCH_MAJOR or entry.is_mla or entry.context_batch_size == 1 or entry.num_heads == 1:
             return entry
         if entry.converted is None:
             from flash_mlm.host.host_utils import convert_batch_major_entry

@@ -404,9 +404,9 @@ def _store_prefill(k, v, q_meta, num_heads, is_mla, block_m, block_n, auto_tune_
     key = str(layer_id)
     k_pk, v_pk = _pack_main_kv(k, v, q_meta, num_heads, is_mla, total_padded, cache.packing,
                                f"layer:{key}:k_cache", f"layer:{key}:v_cache")
-    cache.prefill_kv_cache(layer_id, k_cache=k_pk, v_cache=None if is_mla else v_pk,
-                           total_context_len=int(total_padded), cu_seqlens_kv=q_meta.cu_seqlens,
-                           context_batch_size=int(q_meta.B), is_mla=is_mla, num_heads=num_heads, head_dim=d)
+    cache._store_packed_prefill(layer_id, k_cache=k_pk, v_cache=None if is_mla else v_pk,
+                                total_context_len=int(total_padded), cu_seqlens_kv=q_meta.cu_seqlens,
+                                context_batch_size=int(q_meta.B), is_mla=is_mla, num_heads=num_heads, head_dim=d)
     return k_pk, v_pk, total_padded
 
 
@@ -483,7 +483,8 @@ def flash_attn_mlm_precompressed(
                               owners=(q, k, v))
         del keep
     if prefill and inference_cache is not None:
-        inference_cache.prefill_kv_cache(layer_id, k_cache=k, v_cache=None if is_mla else v,
-                                         total_context_len=int(total_q_len), cu_seqlens_kv=cu_seqlens_q,
-                                         context_batch_size=batch, is_mla=is_mla, num_heads=num_heads, head_dim=d)
+        inference_cache._store_packed_prefill(layer_id, k_cache=k, v_cache=None if is_mla else v,
+                                              total_context_len=int(total_q_len), cu_seqlens_kv=cu_seqlens_q,
+                                              context_batch_size=batch, is_mla=is_mla, num_heads=num_heads,
+                                              head_dim=d)
     return out

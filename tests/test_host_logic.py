@@ -105,8 +105,17 @@ def test_cache_context_uniform_synthesis_and_dense_rule():
                                    is_mla=False, context_batch_size=None, device=CPU, dtype=torch.float32,
                                    compressed=False)
     assert ctx.context_len == 3
-    # a head-major entry serves the dense path in place: [H][3 * 3] rows, entry c at rows 3c of each head
-    assert ctx.layout == "heads_major" and ctx.k_cache is k and ctx.total_context_len == 9
+    # buffers handed to prefill_kv_cache are read as the reference reads them (dense: [C][H][ctx])
+    assert ctx.layout == "batch_major" and ctx.k_cache is k
+    # an entry a packed prefill wrote is head-major and serves the dense path in place:
+    # [H][3 * 3] rows, entry c at rows 3c of each head
+    cache._store_packed_prefill("P", k_cache=k, v_cache=k.clone(), total_context_len=9,
+                                cu_seqlens_kv=torch.tensor([0, 3, 6, 9], dtype=torch.int32), context_batch_size=3,
+                                is_mla=False, num_heads=2, head_dim=4)
+    ctx = _maybe_get_cache_context(inference_cache=cache, layer_id="P", batch_size=3, num_heads=2, head_dim=4,
+                                   is_mla=False, context_batch_size=None, device=CPU, dtype=torch.float32,
+                                   compressed=False)
+    assert ctx.layout == "heads_major" and ctx.context_len == 3 and ctx.total_context_len == 9
 
 
 def test_cache_layouts_seen_by_each_path():
@@ -124,12 +133,12 @@ def test_cache_layouts_seen_by_each_path():
     # MLA and single-head caches have one layout: no conversion is ever needed
     cache._store_dense_prefill(2, k_cache=torch.zeros(6, 8), v_cache=None, context_batch_size=3, is_mla=True,
                                num_heads=4, head_dim=8)
-    assert cache.get_kv_cache(2, is_mla=True, num_heads=4, head_dim=8, dtype=torch.float32,
-                              device=CPU).layout == "heads_major"
+    e2 = cache.get_kv_cache(2, is_mla=True, num_heads=4, head_dim=8, dtype=torch.float32, device=CPU)
+    assert cache.as_heads_major(e2) is e2
     # uneven head-major entries: the dense path refuses them (reference message)
-    cache.prefill_kv_cache(3, k_cache=torch.zeros(2 * 7, 8), v_cache=torch.zeros(2 * 7, 8), total_context_len=7,
-                           cu_seqlens_kv=torch.tensor([0, 2, 7], dtype=torch.int32), context_batch_size=2,
-                           is_mla=False, num_heads=2, head_dim=8)
+    cache._store_packed_prefill(3, k_cache=torch.zeros(2 * 8, 8), v_cache=torch.zeros(2 * 8, 8),
+                                total_context_len=8, cu_seqlens_kv=torch.tensor([0, 2, 8], dtype=torch.int32),
+                                context_batch_size=2, is_mla=False, num_heads=2, head_dim=8)
     with pytest.raises(ValueError, match="requires uniform per-batch context lengths"):
         _maybe_get_cache_context(inference_cache=cache, layer_id=3, batch_size=2, num_heads=2, head_dim=8,
                                  is_mla=False, context_batch_size=None, device=CPU, dtype=torch.float32,
