@@ -50,6 +50,7 @@ struct AttnParams {
   int ctx_bs;       // context batch size
   int ctx_len;      // dense: uniform context length per context batch
   long long t_out;  // packed: rows per head in the output
+  int out_padded;   // packed: output is [B, H, N, D] with zero rows past each sequence (else packed [H*t_out, D])
   int num_items;    // dense: number of work items
   float scale_log2; // scale * log2(e)
   const int* cu_q;  // [B+1] packed query offsets
@@ -209,11 +210,17 @@ struct Seg {
 // role needs dynamically indexed local memory.
 struct Item {
   int qb, qh, qrow0;
-  int dh;  // which DV-wide column block of O this item produces
+  // Bit 0: which DV-wide column block of O this item produces (dh).  Bits
+  // 1-31, padded output only: rows [0, zero_limit) from out_row0 are this
+  // item's to write; rows at or past its valid query rows get zeros (the last
+  // item of a sequence also owns the padding rows up to N); 0 otherwise.
+  int dh_zl;
   int qrows0, qrows1;
   long long out_row0;
   Seg ctx, main;
   __device__ __forceinline__ int qrows(int t) const { return t == 0 ? qrows0 : qrows1; }
+  __device__ __forceinline__ int dh() const { return dh_zl & 1; }
+  __device__ __forceinline__ int zero_limit() const { return dh_zl >> 1; }
   __device__ __forceinline__ int nblocks() const { return ctx.nblk + main.nblk; }
   // Segment and first row of key block j (j counts context blocks first).
   __device__ __forceinline__ Seg block_seg(int j, int bn, int& row) const {
@@ -227,7 +234,7 @@ struct Item {
 template <int PAIR, int BN, int NDH>
 __device__ __forceinline__ Item decode_item(const AttnParams& p, int w) {
   Item it;
-  it.dh = w % NDH;
+  it.dh_zl = w % NDH;
   w /= NDH;
   const int h = w % p.H;
   const int r = w / p.H;
@@ -256,7 +263,12 @@ __device__ __forceinline__ Item decode_item(const AttnParams& p, int w) {
   } else {
     it.qb = p.q_padded ? b : 0;
     it.qrow0 = p.q_padded ? rel0 : seq_start + rel0;
-    it.out_row0 = (long long)h * p.t_out + seq_start + rel0;
+    if (p.out_padded) {
+      it.out_row0 = ((long long)b * p.H + h) * p.N + rel0;
+      it.dh_zl |= ((rel0 + PAIR >= L) ? p.N - rel0 : PAIR) << 1;
+    } else {
+      it.out_row0 = (long long)h * p.t_out + seq_start + rel0;
+    }
   }
   const int kh = p.is_mla ? 0 : h;
   // context segment
@@ -288,6 +300,7 @@ __device__ __forceinline__ Item decode_item(const AttnParams& p, int w) {
   }
   c.nblk = c.row1 > c.row0 ? (c.row1 - c.row0 + BN - 1) / BN : 0;
   m.nblk = m.row1 > m.row0 ? (m.row1 - m.row0 + BN - 1) / BN : 0;
+  if (L == 0) c.nblk = m.nblk = 0;  // an empty sequence's item only writes zero rows (padded output)
   return it;
 }
 
@@ -541,7 +554,7 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
             if (!failed && C::KSPLIT) {
               // long ring: the half this item uses as V (columns dh*256...);
               // short ring: the other half, read only by S.
-              const int hl = it.dh, hs = 1 - it.dh;
+              const int hl = it.dh(), hs = 1 - it.dh();
               uint64_t* lb = fix ? &bar->fix : &bar->k_full[st];
               mbar_arrive_expect_tx(lb, C::KV_BYTES);
               for (int s = 0; s < C::KNSLAB; ++s)
@@ -702,7 +715,7 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
               q1_ph ^= 1u;
             }
             tc_fence_after();
-            issue_s(st1, (g1 & 1u) * BN, ss1, it.dh);
+            issue_s(st1, (g1 & 1u) * BN, ss1, it.dh());
             commit(&bar->s_full[g1 & 1u]);
             if constexpr (C::KSPLIT) commit(&bar->ks_empty[ss1]);
             FMLM_TR(32);
@@ -718,7 +731,7 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
             o_empty_ph ^= 1u;
           }
           tc_fence_after();
-          issue_pv(st, j > 0, it.dh, b * BN);
+          issue_pv(st, j > 0, it.dh(), b * BN);
           commit(&bar->pv_done[0]);
           commit(&bar->kv_empty[st]);
         }
@@ -773,7 +786,7 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
             o_empty_ph ^= 1u;
           }
           tc_fence_after();
-          issue_pv(st, j > 0, it.dh);
+          issue_pv(st, j > 0, it.dh());
           commit(&bar->pv_done[t]);
           commit(&bar->kv_empty[st]);
         } else {
@@ -786,7 +799,7 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
             o_empty_ph ^= 1u;
           }
           tc_fence_after();
-          issue_pv(st, j > 0, it.dh);
+          issue_pv(st, j > 0, it.dh());
           if (j + 1 < nb) {
             if (!wait(&bar->k_full[st1], ph1)) break;
             tc_fence_after();
@@ -829,6 +842,24 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
     Item it;
     for (uint32_t ring = 0; take_item(ring, w, it); ++ring) {
       const int nrows = it.qrows(t);
+      // Padded output: zero the rows of this tile past the sequence's valid
+      // rows, and (tile NQ-1 of a sequence's last item) the padding rows after
+      // the item, up to N.  Each row of [B, H, N, D] is written exactly once.
+      auto zero_pad_rows = [&]() {
+        if (it.zero_limit() == 0) return;
+        T* obase = out + it.out_row0 * (long long)D + it.dh() * C::DV;
+        auto zero_row = [&](int i) {
+          uint4* dst = reinterpret_cast<uint4*>(obase + (long long)i * D);
+#pragma unroll 4
+          for (int q = 0; q < C::DV * 2 / 16; ++q) dst[q] = make_uint4(0, 0, 0, 0);
+        };
+        const int i0 = t * BM + row;
+        if (row >= nrows && i0 < it.zero_limit()) zero_row(i0);
+        if (t == NQ - 1)
+          for (int i = NQ * BM + row; i < it.zero_limit(); i += BM) zero_row(i);
+      };
+      // (before the key loop, so nothing it needs stays live through it)
+      zero_pad_rows();
       if (nrows == 0) continue;
       const bool row_valid = row < nrows;
       const bool pp = kPingPong && it.qrows0 > 0 && it.qrows1 > 0;
@@ -1018,7 +1049,7 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
       FMLM_TR(18 + t);
       tc_fence_after();
       const float inv = (l > 0.f) ? 1.0f / l : 1.0f;
-      T* orow = out + (it.out_row0 + t * BM + row) * (long long)D + it.dh * C::DV;
+      T* orow = out + (it.out_row0 + t * BM + row) * (long long)D + it.dh() * C::DV;
       auto store_chunk = [&](const uint32_t(&o)[OC], int c0) {
         if (!row_valid) return;
         uint32_t v[OC / 2];

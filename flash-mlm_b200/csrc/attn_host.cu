@@ -137,7 +137,7 @@ __global__ void __launch_bounds__(kSchedThreads) sched_kernel(const int* __restr
                                                               const int* __restrict__ cu_kv,
                                                               const int* __restrict__ ctx_index, int B, int ctx_bs,
                                                               int has_ctx, int causal, int pair, int* work,
-                                                              int cap, int* err) {
+                                                              int cap, int* err, int min_items) {
   __shared__ int key[kSortMax];
   __shared__ int order[kSortMax];
   __shared__ int warp_sums[32];
@@ -169,6 +169,7 @@ __global__ void __launch_bounds__(kSchedThreads) sched_kernel(const int* __restr
       atomicExch(err, kErrSeqTooLong);
       n = 0;
     }
+    if (b >= 0 && n < min_items) n = min_items;  // padded output: empty sequences still get their zero rows
     const int ex = block_exclusive_scan(n, warp_sums, &total);
     const int off = running;
     for (int i = 0; i < n; ++i) {
@@ -344,10 +345,12 @@ extern "C" int fmlm_attn_packed_fwd(const fmlm_packed_args* a, void* stream) {
   if (!a->cu_seqlens_q) return set_error(FMLM_ERR_INVALID, "cu_seqlens_q is required");
   if (!a->error_word) return set_error(FMLM_ERR_INVALID, "error_word is required");
   const bool q_padded = a->q_layout == FMLM_LAYOUT_PADDED;
+  const bool out_padded = a->out_padded != 0;
   const bool kv_padded = a->kv_layout == FMLM_LAYOUT_PADDED;
   if (kv_padded && a->causal_query_seq_attn)
     return set_error(FMLM_ERR_INVALID, "causal_query_seq_attn needs packed main k/v");
-  if ((q_padded || kv_padded) && a->seq_len <= 0) return set_error(FMLM_ERR_INVALID, "seq_len required for padded layouts");
+  if ((q_padded || kv_padded || out_padded) && a->seq_len <= 0)
+    return set_error(FMLM_ERR_INVALID, "seq_len required for padded layouts");
   if ((int64_t)a->seq_len > 65535LL * pair_rows(D)) return set_error(FMLM_ERR_INVALID, "sequence too long");
   const bool has_ctx = !a->prefill && a->cu_seqlens_kv != nullptr && a->k_cache.data != nullptr &&
                        a->k_cache.rows > 0;
@@ -378,7 +381,7 @@ extern "C" int fmlm_attn_packed_fwd(const fmlm_packed_args* a, void* stream) {
   if (!a->reuse_schedule) {
     sched_kernel<<<1, kSchedThreads, 0, s>>>(a->cu_seqlens_q, has_ctx ? a->cu_seqlens_kv : a->cu_seqlens_q,
                                              ctx_index, a->batch, a->context_batch_size, has_ctx, a->causal_query_seq_attn, pr,
-                                             work, (int)cap, a->error_word);
+                                             work, (int)cap, a->error_word, out_padded ? 1 : 0);
     if ((rc = check_launch("sched_kernel"))) return rc;
   }
 
@@ -392,6 +395,7 @@ extern "C" int fmlm_attn_packed_fwd(const fmlm_packed_args* a, void* stream) {
   p.B = a->batch; p.H = a->num_heads; p.N = a->seq_len;
   p.ctx_bs = a->context_batch_size;
   p.t_out = a->out_rows_per_head;
+  p.out_padded = out_padded;
   p.scale_log2 = a->scale * 1.4426950408889634f;
   p.cu_q = a->cu_seqlens_q;
   p.cu_kv = has_ctx ? a->cu_seqlens_kv : a->cu_seqlens_q;

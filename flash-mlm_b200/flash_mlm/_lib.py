@@ -85,6 +85,7 @@ class PackedArgs(ctypes.Structure):
         ("error_word", ctypes.c_void_p),
         ("reuse_schedule", ctypes.c_int32),
         ("context_index", ctypes.c_void_p),
+        ("out_padded", ctypes.c_int32),
     ]
 
 

@@ -161,7 +161,7 @@ def flash_attn_mlm(
 
 def _packed_launch(*, q_view, k_view, v_view, q_layout, kv_layout, seq_len, total_q_len, num_heads, batch, d,
                    dtype, is_mla, prefill, causal, ctx, scale, cu_seqlens_q, out, out_rows_per_head, cache, device,
-                   context_index=None, owners=()):
+                   context_index=None, owners=(), out_padded=False):
     total_context_len = int(ctx.total_context_len)
     has_ctx = (not prefill) and total_context_len > 0
     ctx_heads = 1 if is_mla else num_heads
@@ -191,6 +191,7 @@ def _packed_launch(*, q_view, k_view, v_view, q_layout, kv_layout, seq_len, tota
     args.cu_seqlens_q = cu_seqlens_q.data_ptr()
     args.out = out.data_ptr()
     args.out_rows_per_head = out_rows_per_head
+    args.out_padded = int(out_padded)
     L = _lib.lib()
     nbytes = L.fmlm_packed_workspace_bytes(batch, total_q_len, d)
     if cache is not None:
@@ -201,7 +202,7 @@ def _packed_launch(*, q_view, k_view, v_view, q_layout, kv_layout, seq_len, tota
             key_tensors = key_tensors + (context_index,)
         key_scalars = (device.type, device.index, d, batch, num_heads, total_q_len, int(has_ctx), int(causal),
                        context_index is not None,
-                       int(ctx.context_batch_size) if has_ctx else 0)
+                       int(ctx.context_batch_size) if has_ctx else 0, bool(out_padded))
         ws, cached = cache.packing.schedule_workspace(key_tensors, key_scalars, nbytes, device)
         args.reuse_schedule = int(cached)
     else:
@@ -253,6 +254,7 @@ def flash_attn_mlm_compressed(
     prefill: bool = False,
     causal_query_seq_attn: bool = False,
     context_index: torch.Tensor | None = None,
+    out_layout: str = "packed",
 ) -> torch.Tensor:
     """Packed variable-length MLM attention.
 
@@ -272,7 +274,11 @@ def flash_attn_mlm_compressed(
     combined with ``prefill`` or an explicit ``context_batch_size``, and costs
     one device read to range-check the indices.
 
-    Returns the packed output [H * total_tokens, D] in q's dtype.
+    ``out_layout`` (beyond the reference): "packed" returns the packed output
+    [H * total_tokens, D] in q's dtype; "padded" returns [B, H, N, D] with
+    zero rows past each sequence -- what ``unpack_from_kernel`` would make of
+    the packed output, bit for bit -- written directly by the attention
+    kernel's epilogue (no separate unpack pass).
     """
     b, h, n, d = validate_qkv_same_shape_rank4(q, k, v, error_prefix="q/k/v")
     if h != num_heads:
@@ -284,6 +290,9 @@ def flash_attn_mlm_compressed(
     if q_meta.batch_ids_block_n != block_n:
         raise ValueError("q_meta was built with different block_n")
     cu_seqlens_q = q_meta.cu_seqlens
+    if out_layout not in ("packed", "padded"):
+        raise ValueError('out_layout must be "packed" or "padded"')
+    out_padded = out_layout == "padded"
     if context_index is not None:
         if prefill:
             raise ValueError("context_index cannot be combined with prefill=True")
@@ -329,8 +338,13 @@ def flash_attn_mlm_compressed(
     if not is_mla and v.stride(-1) != 1:
         v = v.contiguous()
 
-    out = torch.empty((num_heads * total_tokens, d), dtype=q.dtype, device=q.device)
+    if out_padded:
+        out = torch.empty((b, num_heads, n, d), dtype=q.dtype, device=q.device)
+    else:
+        out = torch.empty((num_heads * total_tokens, d), dtype=q.dtype, device=q.device)
     if total_tokens == 0:
+        if out_padded:
+            out.zero_()
         if prefill and use_layer_cache:
             _store_prefill(k, v, q_meta, num_heads, is_mla, block_m, block_n, auto_tune_tiles, inference_cache,
                            layer_id, d)
@@ -364,7 +378,8 @@ def flash_attn_mlm_compressed(
                           num_heads=num_heads, batch=b, d=d, dtype=q.dtype, is_mla=is_mla, prefill=prefill,
                           causal=causal_query_seq_attn, ctx=ctx, scale=scale, cu_seqlens_q=cu_seqlens_q, out=out,
                           out_rows_per_head=total_tokens, cache=inference_cache, device=q.device,
-                          context_index=context_index, owners=(q, k_view_src, v_view_src))
+                          context_index=context_index, owners=(q, k_view_src, v_view_src),
+                          out_padded=out_padded)
     del keep
     return out
 

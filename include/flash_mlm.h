@@ -96,7 +96,7 @@ typedef struct fmlm_packed_args {
   fmlm_view4 k_cache, v_cache;      /* [H][total_context_len] (MLA: heads = 1) */
   const int32_t* cu_seqlens_q;      /* [batch + 1] */
   const int32_t* cu_seqlens_kv;     /* [>= context_batch_size + 1], or NULL when there is no context */
-  void* out;                        /* [H * out_rows_per_head, D] */
+  void* out;                        /* [H * out_rows_per_head, D], or [batch][H][seq_len][D] (out_padded) */
   int64_t out_rows_per_head;
   void* workspace;                  /* fmlm_packed_workspace_bytes() bytes, 16-byte aligned */
   size_t workspace_bytes;
@@ -108,6 +108,10 @@ typedef struct fmlm_packed_args {
                                        context_batch_size rule.  An index out of range attends no context
                                        and sets the error word.  No counterpart in the reference, whose
                                        README lists index-mapped context batching as planned. */
+  int32_t out_padded;               /* 0: out is packed [H * out_rows_per_head, D] (rows of no sequence are left
+                                       unwritten).  1: out is padded [batch][H][seq_len][D], contiguous, with
+                                       zero rows past each sequence's length: the unpack step
+                                       (src/flash_mlm/host/host_utils.py:587-615) done by the attention epilogue. */
 } fmlm_packed_args;
 
 /* Dense bidirectional attention over [context ++ own sequence]. */

@@ -463,12 +463,14 @@ def test_large_logits_rescale_path(D):
     B, H, N = 2, 2, 640
     dt = torch.float16
     q = _rand((B, H, N, D), dt, g, 3.0)
-    # key norms grow along the sequence (later blocks raise the row max many
-    # times over); keys are clamped to |k| <= 1.5 so that, with MLA where V is
-    # K, |o| < 2 and the raw f16 bound applies unchanged
+    # Key norms grow along the sequence, so later blocks raise the row max many
+    # times over.  Such logits make the softmax nearly one-hot, and then P's
+    # rounding to f16 before P V (as in the reference kernel) costs up to
+    # 2^-11 * |V| per output: keys and values are clamped to |x| <= 1.5
+    # (with MLA V is K), which keeps that under the raw 2e-3 bound.
     ramp = torch.linspace(0.1, 1.0, N).view(1, 1, N, 1)
     k = (torch.randn((B, H, N, D), generator=g) * ramp).clamp(-1.5, 1.5).to(dt)
-    v = k if is_mla else _rand((B, H, N, D), dt, g)
+    v = k if is_mla else torch.randn((B, H, N, D), generator=g).clamp(-1.5, 1.5).to(dt)
     scale = 4.0 / math.sqrt(D)
     out = fm().flash_attn_mlm(q.to(DEV), k.to(DEV), v.to(DEV), scale=scale, is_mla=is_mla)
     ref = oracle.attention_dense(q.float().numpy(), k.float().numpy(), v.float().numpy(), scale, is_mla=is_mla)
@@ -716,4 +718,58 @@ def test_precompressed_vs_oracle(is_mla, causal, dt):
                                   total_context_len=tcl, is_mla=is_mla, causal_query_seq_attn=causal)
     assert out.shape == (H * T, D)
     assert_close_tol(out, ref, dt, f"precompressed mla={is_mla} causal={causal}")
+    no_device_errors()
+
+
+# ----------------------------------------------------------------- padded output written by the epilogue
+
+
+@pytest.mark.parametrize("D,dt,is_mla,causal", [(16, torch.float16, False, False), (64, torch.bfloat16, False, True),
+                                                (128, torch.bfloat16, False, False), (128, torch.float16, True, False),
+                                                (256, torch.float16, False, False), (512, torch.bfloat16, True, True)])
+def test_padded_output_equals_unpacked_packed_output(D, dt, is_mla, causal):
+    """out_layout="padded" is unpack_from_kernel(packed output), bit for bit: data rows,
+    zero rows past each sequence (including empty sequences and rows past the last tile)."""
+    g = torch.Generator().manual_seed(700 + D + is_mla + causal)
+    B, H, N = 6, (2 if D == 512 else 3), 300
+    lengths = torch.tensor([300, 0, 129, 1, 256, 40], dtype=torch.int32)
+    q = _rand((B, H, N, D), dt, g, 0.5)
+    k = _rand((B, H, N, D), dt, g, 0.5)
+    v = _rand((B, H, N, D), dt, g)
+    ctx = torch.tensor([10, 300, 0, 64, 129, 7], dtype=torch.int32)
+    cu_kv = torch.cat([torch.zeros(1, dtype=torch.int32), ctx.cumsum(0).to(torch.int32)])
+    tcl = int(cu_kv[-1])
+    rows = tcl if is_mla else H * tcl
+    kc, vc = _rand((rows, D), dt, g, 0.5), _rand((rows, D), dt, g)
+    cache = fm().InferenceCache()
+    cache.prefill_kv_cache(0, k_cache=kc.to(DEV), v_cache=None if is_mla else vc.to(DEV), total_context_len=tcl,
+                           cu_seqlens_kv=cu_kv.to(DEV), context_batch_size=B, is_mla=is_mla, num_heads=H, head_dim=D)
+    meta = fm().build_pack_metadata(lengths.to(DEV), N, 64)
+    kw = dict(num_heads=H, q_meta=meta, scale=D ** -0.5, inference_cache=cache, layer_id=0, is_mla=is_mla,
+              causal_query_seq_attn=causal, block_n=64)
+    qd, kd, vd = q.to(DEV), k.to(DEV), v.to(DEV)
+    packed = fm().flash_attn_mlm_compressed(qd, kd, vd, **kw)
+    # the padded output over a buffer full of NaN: every position must be written
+    padded = fm().flash_attn_mlm_compressed(qd, kd, vd, out_layout="padded", **kw)
+    assert padded.shape == (B, H, N, D) and padded.dtype == dt
+    assert torch.equal(padded, fm().unpack_from_kernel(packed, meta, H))
+    with pytest.raises(ValueError, match="out_layout"):
+        fm().flash_attn_mlm_compressed(qd, kd, vd, out_layout="bhnd", **kw)
+    no_device_errors()
+
+
+def test_padded_output_overwrites_stale_memory():
+    """Rows past each sequence are written as zeros even when the allocator hands back dirty memory."""
+    g = torch.Generator().manual_seed(81)
+    B, H, N, D, dt = 3, 2, 200, 64, torch.float16
+    lengths = torch.tensor([0, 200, 70], dtype=torch.int32)
+    q, k, v = (_rand((B, H, N, D), dt, g).to(DEV) for _ in range(3))
+    meta = fm().build_pack_metadata(lengths.to(DEV), N, 64)
+    for _ in range(3):
+        junk = torch.full((B, H, N, D), float("nan"), dtype=dt, device=DEV)
+        del junk
+        out = fm().flash_attn_mlm_compressed(q, k, v, num_heads=H, q_meta=meta, scale=0.125, block_n=64,
+                                             out_layout="padded")
+        assert torch.isfinite(out.float()).all()
+        assert bool((out[0] == 0).all()) and bool((out[2, :, 70:] == 0).all())
     no_device_errors()
