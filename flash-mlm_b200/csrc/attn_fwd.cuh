@@ -152,8 +152,20 @@ struct AttnCfg {
   // Q buffers: with two, the next item's Q is loaded while the current item
   // still computes, so its first S is ready when the softmax reaches it.
   static constexpr int QBUF = (CTAS_PER_SM == 2) ? FMLM_QBUF_2CTA : 1;
-  static constexpr int STAGES = (CTAS_PER_SM == 2) ? (QBUF == 2 ? 2 : FMLM_STAGES_2CTA) : (D <= 32) ? 4 : (D <= 64) ? 3 : (D == 512) ? ((TQ && !KSPLIT) ? (BN <= 48 ? 3 : 2) : 3)
+#ifndef FMLM_STAGES_D64_NQ2
+#define FMLM_STAGES_D64_NQ2 3
+#endif
+  static constexpr int STAGES = (CTAS_PER_SM == 2) ? (QBUF == 2 ? 2 : FMLM_STAGES_2CTA) : (D <= 32) ? 4 : (D <= 64) ? FMLM_STAGES_D64_NQ2 : (D == 512) ? ((TQ && !KSPLIT) ? (BN <= 48 ? 3 : 2) : 3)
                               : (D == 128 && BN == 64) ? 4 : 2;
+#ifndef FMLM_POLY_EXP
+#define FMLM_POLY_EXP 0
+#endif
+#ifndef FMLM_POLY_EXP_D128
+#define FMLM_POLY_EXP_D128 0
+#endif
+  // One pair of exponentials in POLY is evaluated on the FMA pipe (0: all on MUFU).
+  static constexpr int POLY = (D <= 64) ? FMLM_POLY_EXP : (D == 128) ? FMLM_POLY_EXP_D128 : 0;
+  static_assert(STAGES >= 1 && STAGES <= 4, "the barrier block holds four K/V stages");
   static constexpr int NUM_SOFTMAX_WARPS = 4 * NQ;
   static constexpr int TMA_WARP = NUM_SOFTMAX_WARPS;
   static constexpr int MMA_WARP = NUM_SOFTMAX_WARPS + 1;  // one MMA-issuing warp per tile: MMA_WARP + t
@@ -175,6 +187,16 @@ struct AttnCfg {
   // (tcgen05 ops of one thread run in order).
   static constexpr bool SDB = TQ;
   static constexpr bool SEP_P = !SDB && NQ * (BN + DV + BN / 2) <= 512;
+#ifndef FMLM_SPLIT_PV
+#define FMLM_SPLIT_PV 0
+#endif
+  // SPLIT_PV (separate P, one tile): P is written and consumed in two halves
+  // of the key block.  The softmax stores half h of P(j) and signals it on
+  // p_full[h]; the MMA warp issues the P V MMAs of that half at once and
+  // commits pv_done[h].  Writing half h of P(j+1) then waits only for half h
+  // of P V(j), which was issued half an exponential loop earlier, so the
+  // P V latency leaves the softmax's critical path.
+  static constexpr bool SPLIT_PV = SEP_P && NQ == 1 && FMLM_SPLIT_PV;
   static constexpr int TM_S = 0;                   // S_t at column t*BN (SDB: buffer b at b*BN)
   static constexpr int TM_O = SDB ? 2 * BN : NQ * BN;  // O_t at column TM_O + t*DV
   static constexpr int TM_P = SEP_P ? NQ * (BN + DV) : 0;  // P_t at TM_P + t*BN/2 (or over S_t)
@@ -652,13 +674,14 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
         }
       }
     };
-    auto issue_pv = [&](int st, bool acc, int dh, uint32_t p_col = 0) {
+    auto issue_pv = [&](int st, bool acc, int dh, uint32_t p_col = 0, int k_lo = 0, int k_hi = -1) {
+      if (k_hi < 0) k_hi = BN / 16;
       if (leader) {
         // V columns [dh*DV, dh*DV + DV) start at slab dh*DV/SLAB_COLS of the tile.
         const uint32_t vbase = C::KSPLIT ? sKa + st * C::KV_BYTES  // the long ring holds exactly the V half
                                : (mla ? sKa : sVa) + st * C::KV_BYTES + (dh * C::DV / C::SLAB_COLS) * (BN * SWB);
 #pragma unroll
-        for (int kk = 0; kk < BN / 16; ++kk) {
+        for (int kk = k_lo; kk < k_hi; ++kk) {
           const uint64_t b = make_smem_desc(vbase + kk * 16 * SWB, BN * SWB, 8 * SWB, layout);
           umma_ts(tO_d, tP_a + p_col + kk * 8, b, idesc_pv, (acc || kk > 0) ? 1u : 0u);
         }
@@ -778,6 +801,26 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
           }
           // ... then O_t += P_t(j) V(j) once P_t(j) is in TMEM.
           if (!mla && !wait(&bar->v_full[st], ph)) break;
+          if constexpr (C::SPLIT_PV) {
+            // each half of P as soon as the softmax has stored it
+            bool ok = true;
+#pragma unroll
+            for (int h = 0; h < 2 && ok; ++h) {
+              if (!wait(&bar->p_full[h], p_ph)) { ok = false; break; }
+              if (h == 0) FMLM_TR(30);
+              if (h == 0 && j == 0) {
+                if (!wait(&bar->o_empty[t], o_empty_ph)) { ok = false; break; }
+                o_empty_ph ^= 1u;
+              }
+              tc_fence_after();
+              issue_pv(st, j > 0, it.dh(), 0, h * (BN / 32), (h + 1) * (BN / 32));
+              commit(&bar->pv_done[h]);
+            }
+            if (!ok) break;
+            p_ph ^= 1u;
+            commit(&bar->kv_empty[st]);
+            continue;
+          }
           if (!wait(&bar->p_full[t], p_ph)) break;
           p_ph ^= 1u;
           if (t == 0) FMLM_TR(30);
@@ -828,6 +871,7 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
     const bool pos_scale = sl2 > 0.f;
     const float fac = pos_scale ? sl2 : 1.0f;
     uint32_t s_ph = 0, o_ph = 0, pv_ph = 0, tok_ph = 0;
+    uint32_t pvh_ph0 = 0, pvh_ph1 = 0;  // SPLIT_PV: phases of pv_done[0] / pv_done[1]
     uint32_t gblk = 0;  // SDB: key blocks processed so far (same count as the MMA warp's)
     T* out = reinterpret_cast<T*>(p.out);
     // With two tiles the exp2 loops of the tiles alternate (a token passed
@@ -835,7 +879,10 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
     // max / TMEM / barrier latency instead of contending with it.  Measured:
     // 17% faster at head_dim 128; slower at 64, where one tile per CTA and
     // two CTAs per SM is used instead.
-    constexpr bool kPingPong = NQ == 2 && D >= 128 && FMLM_PINGPONG;
+#ifndef FMLM_PINGPONG_D64
+#define FMLM_PINGPONG_D64 0
+#endif
+    constexpr bool kPingPong = NQ == 2 && ((D >= 128 && FMLM_PINGPONG) || (D == 64 && FMLM_PINGPONG_D64));
     if (kPingPong && t == 1 && lane == 0) mbar_arrive(&bar->exp_tok[0]);
 
     int w;
@@ -925,7 +972,25 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
             for (int c = 0; c < BN; ++c)
               if (c >= kvv) r[c] = 0xff800000u;  // -inf
           }
+          FMLM_TR(26 + t);
           float mx;
+#if defined(FMLM_MAXMODE) && FMLM_MAXMODE == 2
+          mx = (j == 0) ? 0.f : m / fac;  // timing experiment only: no max
+          mx *= fac;
+#elif defined(FMLM_MAXMODE) && FMLM_MAXMODE == 1
+          {
+            float m16[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) m16[i] = __uint_as_float(r[i]);
+#pragma unroll
+            for (int c = 16; c < BN; ++c) m16[c & 15] = fmaxf(m16[c & 15], __uint_as_float(r[c]));
+#pragma unroll
+            for (int w2 = 8; w2 > 0; w2 >>= 1)
+#pragma unroll
+              for (int i = 0; i < w2; ++i) m16[i] = fmaxf(m16[i], m16[i + w2]);
+            mx = m16[0] * fac;
+          }
+#else
           {
             // 3-input max tree: BN/2 instructions in 8 independent chains.
             float m8[8];
@@ -939,6 +1004,7 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
             mx = fmax3(fmax3(m8[0], m8[1], m8[2]), fmax3(m8[3], m8[4], m8[5]), fmaxf(m8[6], m8[7]));
             mx *= fac;  // -inf stays -inf (fac > 0)
           }
+#endif
           // Move the reference max only when this block raises it by more than 2^8.
           bool need = false;
           float alpha = 1.0f;
@@ -951,6 +1017,76 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
             m = mx;
           }
           const float neg_mu = (m == -INFINITY) ? 0.f : -m;
+          FMLM_TR(22 + t);
+          if constexpr (C::SPLIT_PV) {
+            // Half h of P(j) may be written once half h of P V(j-1) has read
+            // P(j-1).  A rescale of O needs all of P V(j-1) first, and must
+            // land before P V(j) starts (its first half is issued as soon as
+            // half 0 of P(j) is stored), so it comes before the exponentials.
+            bool waited0 = j == 0, waited1 = j == 0;
+            auto wait_half = [&](int h) -> bool {
+              uint32_t& ph = h == 0 ? pvh_ph0 : pvh_ph1;
+              if (!mbar_wait(&bar->pv_done[h], ph, abort_flag, tmo)) fail();
+              failed = __any_sync(0xffffffffu, failed);
+              ph ^= 1u;
+              tc_fence_after();
+              return !failed;
+            };
+            const bool rescale = __any_sync(0xffffffffu, need);
+            FMLM_TR(24 + t);
+            float sums[4] = {0.f, 0.f, 0.f, 0.f};
+            constexpr int HC = BN / 4;  // packed P columns per half
+            bool ok = true;
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              if (!(h == 0 ? waited0 : waited1) && !wait_half(h)) { ok = false; break; }
+              if (h == 1) waited1 = true;
+              uint32_t pk[HC];
+#pragma unroll
+              for (int cc = 0; cc < HC; ++cc) {
+                const int c = h * HC + cc;
+                const float x0 = fmaf(__uint_as_float(r[2 * c]), fac, neg_mu);
+                const float x1 = fmaf(__uint_as_float(r[2 * c + 1]), fac, neg_mu);
+                const float p0 = ex2_approx(x0);
+                const float p1 = ex2_approx(x1);
+                sums[(2 * c) & 3] += p0;
+                sums[(2 * c + 1) & 3] += p1;
+                if constexpr (BF16) {
+                  __nv_bfloat162 v2 = __floats2bfloat162_rn(p0, p1);
+                  pk[cc] = *reinterpret_cast<uint32_t*>(&v2);
+                } else {
+                  __half2 v2 = __floats2half2_rn(p0, p1);
+                  pk[cc] = *reinterpret_cast<uint32_t*>(&v2);
+                }
+              }
+              static_assert(HC == 32 || HC == 16, "SPLIT_PV half width");
+              if constexpr (HC == 32) tmem_st_x32_nowait(tP + h * HC, pk);
+              else tmem_st_x16_nowait(tP + h * HC, pk);
+              if (h == 0 && rescale) {
+                // O holds P V(0..j-1) once both halves of P V(j-1) are done;
+                // it is rescaled before P V(j) (released by p_full[0]) starts.
+                if (!waited1 && !wait_half(1)) { ok = false; break; }
+                waited1 = true;
+#pragma unroll
+                for (int c0 = 0; c0 < C::DV; c0 += 16) {
+                  uint32_t o[16];
+                  tmem_ld_x16(tO + c0, o);
+#pragma unroll
+                  for (int c = 0; c < 16; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
+                  tmem_st_x16(tO + c0, o);
+                }
+              }
+              tmem_wait_st();
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) mbar_arrive(&bar->p_full[h]);
+            }
+            if (!ok) break;
+            l += (sums[0] + sums[1]) + (sums[2] + sums[3]);
+            FMLM_TR(14 + t);
+            FMLM_TR(16 + t);
+            continue;
+          }
           if constexpr (C::SEP_P) {
             // P_t and O_t are free once PV_t(j-1) has completed (almost always
             // by now); waiting first lets each half of P be stored as soon as
@@ -963,6 +1099,7 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
               tc_fence_after();
             }
           }
+          FMLM_TR(24 + t);
           if (pp) {
             if (!mbar_wait(&bar->exp_tok[t], tok_ph, abort_flag, tmo)) fail();
             failed = __any_sync(0xffffffffu, failed);
@@ -981,8 +1118,15 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
               const int c = h0 + cc;
               const float x0 = fmaf(__uint_as_float(r[2 * c]), fac, neg_mu);
               const float x1 = fmaf(__uint_as_float(r[2 * c + 1]), fac, neg_mu);
-              const float p0 = ex2_approx(x0);
-              const float p1 = ex2_approx(x1);
+              // A share of the exponentials (pairs with cc % FMLM_POLY_EXP ==
+              // FMLM_POLY_EXP - 1) runs on the FMA pipe, the rest on MUFU.
+              const bool poly = C::POLY > 0 && (cc % (C::POLY > 0 ? C::POLY : 1)) == (C::POLY > 0 ? C::POLY : 1) - 1;
+#if defined(FMLM_EXPMODE) && FMLM_EXPMODE == 1
+              const float p0 = x0 * 1e-3f, p1 = x1 * 1e-3f;  // timing experiment only: no exponentials
+#else
+              const float p0 = poly ? ex2_poly(x0) : ex2_approx(x0);
+              const float p1 = poly ? ex2_poly(x1) : ex2_approx(x1);
+#endif
               sums[(2 * c) & 3] += p0;
               sums[(2 * c + 1) & 3] += p1;
               if constexpr (BF16) {
@@ -1037,6 +1181,11 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
         const uint32_t gl = gblk + nb - 1;
         gblk += nb;
         if (!mbar_wait(&bar->pv_done[0], gl & 1u, abort_flag, tmo)) fail();
+      } else if constexpr (C::SPLIT_PV) {
+        if (!mbar_wait(&bar->pv_done[0], pvh_ph0, abort_flag, tmo)) fail();
+        if (!mbar_wait(&bar->pv_done[1], pvh_ph1, abort_flag, tmo)) fail();
+        pvh_ph0 ^= 1u;
+        pvh_ph1 ^= 1u;
       } else if constexpr (C::SEP_P) {
         if (!mbar_wait(&bar->pv_done[t], pv_ph, abort_flag, tmo)) fail();
         pv_ph ^= 1u;
