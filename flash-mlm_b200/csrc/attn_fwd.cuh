@@ -791,7 +791,9 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
           // S_t(j+1) as soon as the softmax has read S_t(j) ...
           if (j + 1 < nb) {
             if (!wait(&bar->k_full[st1], ph1)) break;
+            if (t == 0) FMLM_TR(36);
             if (!wait(&bar->s_free[t], s_free_ph)) break;
+            if (t == 0) FMLM_TR(38);
             s_free_ph ^= 1u;
             tc_fence_after();
             issue_s(st1);
@@ -832,6 +834,7 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
           issue_pv(st, j > 0, it.dh());
           commit(&bar->pv_done[t]);
           commit(&bar->kv_empty[st]);
+          if (t == 0) FMLM_TR(44);
         } else {
           if (!mla && !wait(&bar->v_full[st], ph)) break;
           if (!wait(&bar->p_full[t], p_ph)) break;
@@ -1109,7 +1112,10 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
           float sums[4] = {0.f, 0.f, 0.f, 0.f};
           // P in chunks of up to 32 packed columns (64 scores), each stored to
           // TMEM as soon as it is ready, so at most one chunk of packed P is live.
-          constexpr int PC = BN / 2 < 32 ? BN / 2 : 32;
+#ifndef FMLM_PCHUNK
+#define FMLM_PCHUNK 32
+#endif
+          constexpr int PC = BN / 2 < FMLM_PCHUNK ? BN / 2 : FMLM_PCHUNK;
 #pragma unroll
           for (int h0 = 0; h0 < BN / 2; h0 += PC) {
             uint32_t pk[PC];
@@ -1139,7 +1145,8 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
             }
             if constexpr (PC == 32) tmem_st_x32_nowait(tPb + h0, pk);
             else if constexpr (PC == 24) tmem_st_x24_nowait(tPb + h0, pk);
-            else tmem_st_x16_nowait(tPb + h0, pk);
+            else if constexpr (PC == 16) tmem_st_x16_nowait(tPb + h0, pk);
+            else tmem_st_x8_nowait(tPb + h0, pk);
           }
           if (pp) {
             __syncwarp();

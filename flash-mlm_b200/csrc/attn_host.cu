@@ -202,7 +202,11 @@ int launch_attn(const CUtensorMap* m, const AttnParams& p, long long items, cuda
   auto kern = attn_fwd_kernel<D, NQ, BF16>;
   // Shared memory is padded so that exactly CTAS_PER_SM CTAs (TMEM owners)
   // fit on an SM: more would block in tcgen05.alloc.
+#ifdef FMLM_ONE_CTA_PER_SM  // experiment: one resident CTA per SM whatever the layout
+  const int smem = std::max(C::SMEM_BYTES, 150 * 1024);
+#else
   const int smem = C::CTAS_PER_SM == 1 ? std::max(C::SMEM_BYTES, 116 * 1024) : std::max(C::SMEM_BYTES, 80 * 1024);
+#endif
   static bool configured[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
