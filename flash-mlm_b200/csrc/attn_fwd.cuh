@@ -957,12 +957,22 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
           else if constexpr (BN == 48) tmem_ld_x48(tSb, r);
           else tmem_ld_x32(tSb, r);
           FMLM_TR(12 + t);
-          if constexpr (C::SEP_P) {
-            // S_t is in registers: the MMA warp may overwrite it with S_t(j+1).
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&bar->s_free[t]);
-          }
+#ifndef FMLM_LATE_SFREE
+#define FMLM_LATE_SFREE 0
+#endif
+          // S_t is in registers: the MMA warp may overwrite it with S_t(j+1).
+          // (LATE_SFREE: signalled after the row max instead, so the signal's
+          // latency overlaps the exponentials rather than preceding the max.)
+          auto release_s = [&]() {
+            if constexpr (C::SEP_P) {
+#if !defined(FMLM_SFREE_NOFENCE)
+              tc_fence_before();
+#endif
+              __syncwarp();
+              if (lane == 0) mbar_arrive(&bar->s_free[t]);
+            }
+          };
+          if (!FMLM_LATE_SFREE) release_s();
           // With a positive scale the row max is taken on raw scores and the
           // scale is folded into the exp2 argument (one FFMA per element);
           // otherwise scores are scaled first.
@@ -1020,6 +1030,7 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
             m = mx;
           }
           const float neg_mu = (m == -INFINITY) ? 0.f : -m;
+          if (FMLM_LATE_SFREE) release_s();
           FMLM_TR(22 + t);
           if constexpr (C::SPLIT_PV) {
             // Half h of P(j) may be written once half h of P V(j-1) has read
