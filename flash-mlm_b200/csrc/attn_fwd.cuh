@@ -166,6 +166,15 @@ struct AttnCfg {
   // One pair of exponentials in POLY is evaluated on the FMA pipe (0: all on MUFU).
   static constexpr int POLY = (D <= 64) ? FMLM_POLY_EXP : (D == 128) ? FMLM_POLY_EXP_D128 : 0;
   static_assert(STAGES >= 1 && STAGES <= 4, "the barrier block holds four K/V stages");
+#ifndef FMLM_SPLIT_KV
+#define FMLM_SPLIT_KV 0
+#endif
+  // SPLIT_KV (separate K and V tiles): a K stage is released as soon as the S
+  // that read it completes (k_empty) and a V stage when its P V completes
+  // (kv_empty), and the producer requests V one block behind K, so K(j) is
+  // requested about one block earlier than with a shared release after P V.
+  // (With MLA at run time the K tile is also V: it is released after P V.)
+  static constexpr bool SPLIT_KV = FMLM_SPLIT_KV && D != 512;
   static constexpr int NUM_SOFTMAX_WARPS = 4 * NQ;
   static constexpr int TMA_WARP = NUM_SOFTMAX_WARPS;
   static constexpr int MMA_WARP = NUM_SOFTMAX_WARPS + 1;  // one MMA-issuing warp per tile: MMA_WARP + t
@@ -330,7 +339,7 @@ static_assert(sizeof(Item) <= 96, "item ring slot");
 
 struct __align__(8) AttnBarriers {
   uint64_t q_full[2], q_empty[2], fix;
-  uint64_t k_full[4], v_full[4], kv_empty[4];
+  uint64_t k_full[4], v_full[4], kv_empty[4], k_empty[4];
   uint64_t s_full[2], p_full[2], o_full[2], o_empty[2];
   uint64_t s_free[2], pv_done[2];  // separate-P pipeline only
   uint64_t item_full[4], item_empty[4];  // ring of work-item indices, producer -> other roles
@@ -407,6 +416,7 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
       mbar_init(&bar->k_full[s], 1);
       mbar_init(&bar->v_full[s], 1);
       mbar_init(&bar->kv_empty[s], NQ);
+      mbar_init(&bar->k_empty[s], NQ);
     }
     for (int t = 0; t < 2; ++t) {
       mbar_init(&bar->s_full[t], 1);
@@ -552,60 +562,68 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
       const uint32_t qn_par = (((ring + 1) / C::QBUF) & 1u) ^ 1u;
       const Item itn = (next < num_items) ? decode_item<C::PAIR, BN, C::NDH>(p, next) : it;
       const int nb = it.nblocks();
-      for (int j = 0; j < nb && !failed; ++j, ++fill) {
-        {
+      if constexpr (C::SPLIT_KV) {
+        // K(j) is requested when its stage's previous K has been read by S;
+        // V(j) one block later, when its stage's previous V has been read by
+        // P V.  A partial padded tile is cleared before the next stage wait.
+        struct VJob {
+          int row, h, b, map, st, valid;
+          uint32_t ph;
+          bool fix;
+        };
+        VJob pv{};
+        bool have_pv = false;
+        auto issue_v = [&](const VJob& vj) {
+          resolve_fix();
+          if (!mbar_wait(&bar->kv_empty[vj.st], vj.ph ^ 1u, abort_flag, tmo)) fail();
+          failed = __any_sync(0xffffffffu, failed);
+          uint8_t* tv = sV + vj.st * C::KV_BYTES;
+          if (lane == 0 && !failed) {
+            const CUtensorMap* mv = vj.map == 0 ? &tm_vc : &tm_v;
+            uint64_t* vb = vj.fix ? &bar->fix : &bar->v_full[vj.st];
+            mbar_arrive_expect_tx(vb, C::KV_BYTES);
+            for (int s = 0; s < C::NSLAB; ++s)
+              tma_load_4d(tv + s * (BN * SWB), mv, vb, s * C::SLAB_COLS, vj.row, vj.h, vj.b);
+          }
+          failed = __shfl_sync(0xffffffffu, failed, 0);
+          if (vj.fix && !failed) {
+            pend_tile = tv;
+            pend_valid = vj.valid;
+            pend_bar = &bar->v_full[vj.st];
+          }
+        };
+        for (int j = 0; j < nb && !failed; ++j, ++fill) {
           int row;
           const Seg sgm = it.block_seg(j, BN, row);
           const CUtensorMap* mk = sgm.map == 0 ? &tm_kc : &tm_k;
-          const CUtensorMap* mv = sgm.map == 0 ? &tm_vc : &tm_v;
           const int st = fill % STAGES;
           const uint32_t ph = (fill / STAGES) & 1u;
           const int valid = min(BN, sgm.row1 - row);
           const bool fix = sgm.fix && valid < BN;
           uint8_t* tk = sK + st * C::KV_BYTES;
-          uint8_t* tv = sV + st * C::KV_BYTES;
           resolve_fix();
-          if (!mbar_wait(&bar->kv_empty[st], ph ^ 1u, abort_flag, tmo)) fail();
-          const int ss = fill % 2;
-          if constexpr (C::KSPLIT) {
-            if (!mbar_wait(&bar->ks_empty[ss], ((fill / 2) & 1u) ^ 1u, abort_flag, tmo)) fail();
-          }
+          if (!mbar_wait(&bar->k_empty[st], ph ^ 1u, abort_flag, tmo)) fail();
           failed = __any_sync(0xffffffffu, failed);
-          if (lane == 0) {
+          if (lane == 0 && !failed) {
             FMLM_TR(40);
-            if (!failed && C::KSPLIT) {
-              // long ring: the half this item uses as V (columns dh*256...);
-              // short ring: the other half, read only by S.
-              const int hl = it.dh(), hs = 1 - it.dh();
-              uint64_t* lb = fix ? &bar->fix : &bar->k_full[st];
-              mbar_arrive_expect_tx(lb, C::KV_BYTES);
-              for (int s = 0; s < C::KNSLAB; ++s)
-                tma_load_4d(tk + s * (BN * SWB), mk, lb, (hl * C::KNSLAB + s) * C::SLAB_COLS, row, sgm.h, sgm.b);
-              uint8_t* ts = sKs + ss * C::KV_BYTES;
-              mbar_arrive_expect_tx(&bar->v_full[ss], C::KV_BYTES);
-              for (int s = 0; s < C::KNSLAB; ++s)
-                tma_load_4d(ts + s * (BN * SWB), mk, &bar->v_full[ss], (hs * C::KNSLAB + s) * C::SLAB_COLS, row, sgm.h,
-                            sgm.b);
-            } else if (!failed) {
-              if (!(fix && mla)) {
-                mbar_arrive_expect_tx(&bar->k_full[st], C::KV_BYTES);
-                for (int s = 0; s < C::NSLAB; ++s)
-                  tma_load_4d(tk + s * (BN * SWB), mk, &bar->k_full[st], s * C::SLAB_COLS, row, sgm.h, sgm.b);
-              }
-              if (fix) {
-                uint8_t* tf = mla ? tk : tv;
-                const CUtensorMap* mf = mla ? mk : mv;
-                mbar_arrive_expect_tx(&bar->fix, C::KV_BYTES);
-                for (int s = 0; s < C::NSLAB; ++s)
-                  tma_load_4d(tf + s * (BN * SWB), mf, &bar->fix, s * C::SLAB_COLS, row, sgm.h, sgm.b);
-              } else if (!mla) {
-                mbar_arrive_expect_tx(&bar->v_full[st], C::KV_BYTES);
-                for (int s = 0; s < C::NSLAB; ++s)
-                  tma_load_4d(tv + s * (BN * SWB), mv, &bar->v_full[st], s * C::SLAB_COLS, row, sgm.h, sgm.b);
-              }
-            }
+            // with MLA the K tile is also V: a partial padded one is cleared
+            uint64_t* kb = (fix && mla) ? &bar->fix : &bar->k_full[st];
+            mbar_arrive_expect_tx(kb, C::KV_BYTES);
+            for (int s = 0; s < C::NSLAB; ++s)
+              tma_load_4d(tk + s * (BN * SWB), mk, kb, s * C::SLAB_COLS, row, sgm.h, sgm.b);
           }
           failed = __shfl_sync(0xffffffffu, failed, 0);
+          if (fix && mla && !failed) {
+            pend_tile = tk;
+            pend_valid = valid;
+            pend_bar = &bar->k_full[st];
+            resolve_fix();
+          }
+          if (!mla && !failed) {
+            if (have_pv) issue_v(pv);
+            pv = VJob{row, sgm.h, sgm.b, sgm.map, st, valid, ph, fix};
+            have_pv = true;
+          }
           if (want_next && !q_pre && !failed) {
             bool ready = false;
             if (lane == 0) ready = mbar_test_wait(smem_u32(&bar->q_empty[qn]), qn_par);
@@ -614,13 +632,79 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
               q_pre = true;
             }
           }
-          if (fix && !failed) {
-            pend_tile = mla ? tk : tv;
-            pend_valid = valid;
-            pend_bar = mla ? &bar->k_full[st] : &bar->v_full[st];
-            // With MLA the cleared tile is K, which this item's last S (and so
-            // the release of the Q buffer the next item waits for) needs.
-            if (mla) resolve_fix();
+        }
+        if (have_pv && !failed) issue_v(pv);
+      } else {
+        for (int j = 0; j < nb && !failed; ++j, ++fill) {
+          {
+            int row;
+            const Seg sgm = it.block_seg(j, BN, row);
+            const CUtensorMap* mk = sgm.map == 0 ? &tm_kc : &tm_k;
+            const CUtensorMap* mv = sgm.map == 0 ? &tm_vc : &tm_v;
+            const int st = fill % STAGES;
+            const uint32_t ph = (fill / STAGES) & 1u;
+            const int valid = min(BN, sgm.row1 - row);
+            const bool fix = sgm.fix && valid < BN;
+            uint8_t* tk = sK + st * C::KV_BYTES;
+            uint8_t* tv = sV + st * C::KV_BYTES;
+            resolve_fix();
+            if (!mbar_wait(&bar->kv_empty[st], ph ^ 1u, abort_flag, tmo)) fail();
+            const int ss = fill % 2;
+            if constexpr (C::KSPLIT) {
+              if (!mbar_wait(&bar->ks_empty[ss], ((fill / 2) & 1u) ^ 1u, abort_flag, tmo)) fail();
+            }
+            failed = __any_sync(0xffffffffu, failed);
+            if (lane == 0) {
+              FMLM_TR(40);
+              if (!failed && C::KSPLIT) {
+                // long ring: the half this item uses as V (columns dh*256...);
+                // short ring: the other half, read only by S.
+                const int hl = it.dh(), hs = 1 - it.dh();
+                uint64_t* lb = fix ? &bar->fix : &bar->k_full[st];
+                mbar_arrive_expect_tx(lb, C::KV_BYTES);
+                for (int s = 0; s < C::KNSLAB; ++s)
+                  tma_load_4d(tk + s * (BN * SWB), mk, lb, (hl * C::KNSLAB + s) * C::SLAB_COLS, row, sgm.h, sgm.b);
+                uint8_t* ts = sKs + ss * C::KV_BYTES;
+                mbar_arrive_expect_tx(&bar->v_full[ss], C::KV_BYTES);
+                for (int s = 0; s < C::KNSLAB; ++s)
+                  tma_load_4d(ts + s * (BN * SWB), mk, &bar->v_full[ss], (hs * C::KNSLAB + s) * C::SLAB_COLS, row, sgm.h,
+                              sgm.b);
+              } else if (!failed) {
+                if (!(fix && mla)) {
+                  mbar_arrive_expect_tx(&bar->k_full[st], C::KV_BYTES);
+                  for (int s = 0; s < C::NSLAB; ++s)
+                    tma_load_4d(tk + s * (BN * SWB), mk, &bar->k_full[st], s * C::SLAB_COLS, row, sgm.h, sgm.b);
+                }
+                if (fix) {
+                  uint8_t* tf = mla ? tk : tv;
+                  const CUtensorMap* mf = mla ? mk : mv;
+                  mbar_arrive_expect_tx(&bar->fix, C::KV_BYTES);
+                  for (int s = 0; s < C::NSLAB; ++s)
+                    tma_load_4d(tf + s * (BN * SWB), mf, &bar->fix, s * C::SLAB_COLS, row, sgm.h, sgm.b);
+                } else if (!mla) {
+                  mbar_arrive_expect_tx(&bar->v_full[st], C::KV_BYTES);
+                  for (int s = 0; s < C::NSLAB; ++s)
+                    tma_load_4d(tv + s * (BN * SWB), mv, &bar->v_full[st], s * C::SLAB_COLS, row, sgm.h, sgm.b);
+                }
+              }
+            }
+            failed = __shfl_sync(0xffffffffu, failed, 0);
+            if (want_next && !q_pre && !failed) {
+              bool ready = false;
+              if (lane == 0) ready = mbar_test_wait(smem_u32(&bar->q_empty[qn]), qn_par);
+              if (__shfl_sync(0xffffffffu, ready, 0)) {
+                issue_q(itn, qn);
+                q_pre = true;
+              }
+            }
+            if (fix && !failed) {
+              pend_tile = mla ? tk : tv;
+              pend_valid = valid;
+              pend_bar = mla ? &bar->k_full[st] : &bar->v_full[st];
+              // With MLA the cleared tile is K, which this item's last S (and so
+              // the release of the Q buffer the next item waits for) needs.
+              if (mla) resolve_fix();
+            }
           }
         }
       }
@@ -712,7 +796,14 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
         if (leader) mbar_arrive(q_empty);
         for (int j = 0; j < nb; ++j) {
           const int st = (fill + j) % STAGES;
-          if (!wait(&bar->k_full[st], ((fill + j) / STAGES) & 1u)) break;
+          const uint32_t ph = ((fill + j) / STAGES) & 1u;
+          if (!wait(&bar->k_full[st], ph)) break;
+          if constexpr (C::SPLIT_KV) {
+            if (leader) mbar_arrive(&bar->k_empty[st]);
+            // the V stage is released only once this block's V has landed, so
+            // the release cannot count toward the stage's previous use
+            if (!mla && !wait(&bar->v_full[st], ph)) break;
+          }
           if (leader) mbar_arrive(&bar->kv_empty[st]);
         }
         fill += nb;
@@ -780,6 +871,7 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
         tc_fence_after();
         issue_s(st);
         commit(&bar->s_full[t]);
+        if (C::SPLIT_KV && !mla) commit(&bar->k_empty[st]);
         if (nb == 1) commit(q_empty);
       }
       for (int j = 0; j < nb && !failed; ++j) {
@@ -798,6 +890,7 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
             tc_fence_after();
             issue_s(st1);
             commit(&bar->s_full[t]);
+            if (C::SPLIT_KV && !mla) commit(&bar->k_empty[st1]);
             if (t == 0) FMLM_TR(32);
             if (j + 2 == nb) commit(q_empty);
           }
@@ -821,6 +914,7 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
             if (!ok) break;
             p_ph ^= 1u;
             commit(&bar->kv_empty[st]);
+            if (C::SPLIT_KV && mla) commit(&bar->k_empty[st]);  // MLA: the K tile was also V
             continue;
           }
           if (!wait(&bar->p_full[t], p_ph)) break;
@@ -834,6 +928,7 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
           issue_pv(st, j > 0, it.dh());
           commit(&bar->pv_done[t]);
           commit(&bar->kv_empty[st]);
+          if (C::SPLIT_KV && mla) commit(&bar->k_empty[st]);  // MLA: the K tile was also V
           if (t == 0) FMLM_TR(44);
         } else {
           if (!mla && !wait(&bar->v_full[st], ph)) break;
@@ -851,12 +946,14 @@ __global__ void __launch_bounds__(AttnCfg<D, NQ>::THREADS) __maxnreg__((AttnCfg<
             tc_fence_after();
             issue_s(st1);
             commit(&bar->s_full[t]);
+            if (C::SPLIT_KV && !mla) commit(&bar->k_empty[st1]);
             if (t == 0) FMLM_TR(32);
           } else {
             commit(&bar->o_full[t]);
           }
           if (j + 2 == nb) commit(q_empty);
           commit(&bar->kv_empty[st]);
+          if (C::SPLIT_KV && mla) commit(&bar->k_empty[st]);  // MLA: the K tile was also V
         }
       }
       fill += nb;
