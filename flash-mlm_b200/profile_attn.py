@@ -10,9 +10,10 @@ D=64 bf16 + shared 1024 context; 4 MLA B=16 H=128 D=512 + 4096 context per
 sequence; 3 packed causal B=64 H=12 N=256 D=64 f16 +
 per-sequence context U[256,2048]; 5a packed B=8 H=16 N=512 D=128 bf16 +
 per-sequence context --ctx; 5b packed B=--batch H=16 N=512 D=128 bf16, no context.
-`--op pack` / `--op unpack` run the packing kernels on config 2's shapes
-instead (pack_and_pad_main_tensors_for_mlm_compressed of q/k/v, and
-unpack_from_kernel of a packed [H*T, D] output).
+`--op pack` / `--op unpack` / `--op append` run the copy kernels on config
+2's shapes instead (pack_and_pad_main_tensors_for_mlm_compressed of q/k/v,
+unpack_from_kernel of a packed [H*T, D] output, and InferenceCache
+append_kv_cache of the batch's K/V into a reserved cache).
 Equivalent of the reference's src/profile/profile_mlm_ncu.py.
 """
 
@@ -101,6 +102,17 @@ def build_pack_op(op: str, device):
     B, H, N, D = 32, 16, 512, 64
     lengths = _lengths(g, B, 64, 512)
     meta = flash_mlm.build_pack_metadata(lengths.to(device), N, 64)
+    if op == "append":
+        # append the batch's K/V as 32 new entries of a reserved cache, emptied before each call
+        k, v = (torch.randn((B, H, N, D), generator=g).to(torch.bfloat16).to(device) for _ in range(2))
+        cache = flash_mlm.InferenceCache()
+        cache.reserve_kv_cache(0, capacity=meta.total_tokens, max_entries=B, is_mla=False, num_heads=H, head_dim=D,
+                               dtype=torch.bfloat16, device=device)
+
+        def step():
+            cache.reset_kv_cache(0)
+            cache.append_kv_cache(0, k, v, meta)
+        return step
     if op == "pack":
         q, k, v = (torch.randn((B, H, N, D), generator=g).to(torch.bfloat16).to(device) for _ in range(3))
         return lambda: host_utils.pack_and_pad_main_tensors_for_mlm_compressed(q, k, v, q_meta=meta, num_heads=H,
@@ -111,7 +123,7 @@ def build_pack_op(op: str, device):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--op", default="attn", choices=["attn", "pack", "unpack"])
+    ap.add_argument("--op", default="attn", choices=["attn", "pack", "unpack", "append"])
     ap.add_argument("--config", default="2")
     ap.add_argument("--ctx", type=int, default=4096)
     ap.add_argument("--batch", type=int, default=32)
