@@ -105,3 +105,45 @@ def test_plan_balances_by_cost_and_is_deterministic():
     plans_h = plan_shards(lengths, 16, 4)
     assert [p.heads for p in plans_h] == [(0, 4), (4, 8), (8, 12), (12, 16)]
     assert plan_shards(lengths, 12, 8, context_lengths=[1000] * 8) == plans
+
+
+def test_plan_modes_uneven_heads_and_causal_rules():
+    lengths = [30, 10, 50, 20, 40]
+    # heads split as evenly as the count allows (12 heads over 8 ranks: 1 or 2 each, contiguous)
+    plans = plan_shards(lengths, 12, 8, mode="heads")
+    sizes = [p.heads[1] - p.heads[0] for p in plans]
+    assert sorted(set(sizes)) == [1, 2] and sum(sizes) == 12
+    assert all(plans[r].heads[1] == plans[r + 1].heads[0] for r in range(7))
+    assert all(p.batches == list(range(5)) for p in plans)
+    # a causal job reads earlier sequences' keys: always split by heads, even when asked for batch
+    assert all(p.mode == "heads" for p in plan_shards(lengths, 12, 4, causal=True, mode="batch"))
+    # auto: heads when they divide, sequences otherwise; MLA always by sequences
+    assert plan_shards(lengths, 16, 4)[0].mode == "heads"
+    assert plan_shards(lengths, 12, 8)[0].mode == "batch"
+    mla = plan_shards(lengths, 16, 2, is_mla=True, context_lengths=[5] * 5)
+    assert {p.mode for p in mla} == {"batch"} and sorted(b for p in mla for b in p.batches) == list(range(5))
+    with pytest.raises(ValueError, match="MLA with causal"):
+        plan_shards(lengths, 16, 2, is_mla=True, causal=True)
+    with pytest.raises(ValueError, match="at least one head per rank"):
+        plan_shards(lengths, 4, 8, mode="heads")
+    with pytest.raises(ValueError, match="mode must be"):
+        plan_shards(lengths, 4, 2, mode="rows")
+
+
+def test_bench_shards_cover_the_job():
+    """bench.py's per-rank workloads: weak scaling grows the job N times, strong splits it; the
+    ranks' shards cover every (sequence, head) of the job exactly once."""
+    import argparse
+
+    import bench
+
+    args = argparse.Namespace(ctx=4096, batch=32)
+    one = bench.Workload("2", args)
+    strong = [bench.Workload("2", args, rank=r, world=4, scaling="strong") for r in range(4)]
+    assert sum(w.H * w.T for w in strong) == one.H * one.T  # every (token, head) once
+    assert sum(w.flops() for w in strong) == pytest.approx(one.flops())
+    weak = [bench.Workload("2", args, rank=r, world=4, scaling="weak") for r in range(4)]
+    assert sum(w.B for w in weak) == 4 * one.B and weak[0].B_job == 4 * one.B
+    assert sorted(b for w in weak for b in w.plan.batches) == list(range(4 * one.B))
+    causal = [bench.Workload("3", args, rank=r, world=2, scaling="weak") for r in range(2)]
+    assert all(w.plan.mode == "heads" and w.H == 12 and w.B == 64 for w in causal)
