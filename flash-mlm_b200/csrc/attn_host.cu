@@ -322,8 +322,12 @@ extern "C" int fmlm_attn_dense_fwd(const fmlm_dense_args* a, void* stream) {
 
 // Packed launches at head_dim 128 use single-tile items when the problem has
 // fewer tile pairs than the GPU has SMs.
+#ifndef FMLM_SINGLE_TILE_FACTOR
+#define FMLM_SINGLE_TILE_FACTOR 1
+#endif
 bool packed_single_tile(int D, int64_t total_q_len, int batch, int heads) {
-  return D == 128 && (total_q_len / pair_rows(D) + batch) * (int64_t)heads < device_sm_count();
+  return D == 128 &&
+         (total_q_len / pair_rows(D) + batch) * (int64_t)heads < (int64_t)FMLM_SINGLE_TILE_FACTOR * device_sm_count();
 }
 
 extern "C" size_t fmlm_packed_workspace_bytes(int32_t batch, int64_t total_q_len, int32_t head_dim) {
