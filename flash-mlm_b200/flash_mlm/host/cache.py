@@ -378,7 +378,10 @@ class InferenceCache:
         """Give a layer a head-major cache of ``capacity`` rows per head and room
         for ``max_entries`` context entries.  Later ``append_kv_cache`` calls,
         and ``prefill=True`` calls of the packed launchers, write into it on the
-        device instead of allocating; the layer's entry is empty until then."""
+        device instead of allocating; the layer's entry is empty until then.
+        (The dense launcher's prefill and ``flash_attn_mlm_precompressed``'s
+        prefill store their own buffers, as in the reference, replacing the
+        entry; the reservation stays for later appends.)"""
         if capacity < 0 or max_entries < 1 or num_heads < 1:
             raise ValueError("capacity must be >= 0, max_entries >= 1 and num_heads >= 1")
         rows = capacity if is_mla else num_heads * capacity
